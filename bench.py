@@ -1,0 +1,413 @@
+#!/usr/bin/env python3
+"""Benchmark of the fused W8A8 INT8 linear on B200.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one pass of the hot path over one batch: fp16 activations
+X[4096,3072] (1% outlier channels x20) -> block-128 Hadamard rotation +
+per-token INT8 quantization (prologue kernel) -> tcgen05 kind::i8 GEMM
+against the rotated, per-channel-quantized weight W[12288,3072] with the
+fused scale/bias/fp16 epilogue.  Metric: TOPS = 2*M*N*K / step time.
+
+Multi-GPU (torchrun, one rank per GPU, NCCL): column-parallel N-sharding with
+weak scaling -- every rank owns a [12288,3072] column shard of a
+[12288*P,3072] weight and computes its [4096,12288] output block from the
+replicated activations.  The NCCL all-gather that reassembles the full output
+is timed separately and reported under "allgather" (it is not needed by a
+consumer that reads the sharded output).
+
+The reference arm (--impl reference) times the CPU oracle -- the reference's
+math restated in C (oracle/) -- on the host cores over a bounded sample of
+the same workload.
+"""
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "rdna2-gfx1030-ai-handbook_b200"))
+
+M, K, N = 4096, 3072, 12288
+ROT = 128
+METRIC = "INT8 fused-GEMM TOPS & % of tensor peak at 1/2/4/8 B200 vs host-CPU ref"
+UNIT = "TOPS"
+SEED = 20261106
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--cpu-budget-s", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sets", type=int, default=4, help="input sets cycled to defeat L2 reuse")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"bf16_tflops": d["bf16_tflops"], "bf16_tflops_sustained": d["bf16_tflops_sustained"],
+                "hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0,
+            "source": "fallback"}
+
+
+def synth_inputs(rng, m, k):
+    x = rng.standard_normal((m, k), dtype=np.float32)
+    idx = rng.choice(k, size=max(1, round(0.01 * k)), replace=False)
+    x[:, idx] *= 20.0
+    return x
+
+
+# ------------------------------------------------------------- CPU oracle
+def cpu_run(rows, threads=0):
+    """Time the oracle's full W8A8 linear on `rows` tokens of the workload."""
+    import oracle
+    rng = np.random.default_rng(SEED)
+    x = synth_inputs(rng, rows, K).astype(np.float16).view(np.uint16)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02))
+    wq, sw = oracle.quant_rows_int8(oracle.rotate_rows(w, oracle.F32, ROT))
+    bias = oracle.encode((rng.standard_normal(N) * 0.02).astype(np.float32), oracle.F16)
+    t0 = time.perf_counter()
+    oracle.w8a8_linear(x, oracle.F16, ROT, wq, sw, bias, oracle.F16, oracle.EPI_SEPARATE,
+                       oracle.F16, threads=threads)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(budget_s):
+    import oracle
+    threads = oracle.max_threads()
+    t1 = cpu_run(64, threads)
+    rows = int(min(M, max(64, budget_s / max(t1 / 64, 1e-9))))
+    rows = max(64, rows // 64 * 64)
+    dt = cpu_run(rows, threads)
+    return {"value": round(2.0 * rows * N * K / dt / 1e12, 4), "unit": UNIT, "cores": threads,
+            "kind": "port",
+            "sample": f"oracle/qlinear_oracle.c w8a8 linear (rotate+quantize+exact GEMM+epilogue) "
+                      f"on {rows} of {M} tokens x N={N} x K={K}, {dt:.2f} s, {threads} OpenMP threads"}
+
+
+def run_reference(args, rank):
+    """--impl reference: the CPU oracle port on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    import oracle
+    threads = oracle.max_threads()
+    t1 = cpu_run(64, threads)
+    per_row = t1 / 64
+    budget = 120.0 / max(1, args.steps + args.warmup)
+    rows = int(min(M, max(8, budget / per_row)))
+    import oracle as o
+    rng = np.random.default_rng(SEED)
+    x = synth_inputs(rng, rows, K).astype(np.float16).view(np.uint16)
+    w = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
+    wq, sw = o.quant_rows_int8(o.rotate_rows(w, o.F32, ROT))
+    bias = o.encode((rng.standard_normal(N) * 0.02).astype(np.float32), o.F16)
+
+    def step():
+        o.w8a8_linear(x, o.F16, ROT, wq, sw, bias, o.F16, o.EPI_SEPARATE, o.F16, threads=threads)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / max(1, args.steps)
+    value = 2.0 * rows * N * K / dt / 1e12
+    line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic", "impl": "reference",
+            "config": {"workload": "config2 W8A8 rotated linear, CPU sample",
+                       "M": M, "N": N, "K": K, "rotation_block": ROT, "sample_rows": rows},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
+                             "kind": "port",
+                             "sample": f"{rows} of {M} tokens per step (oracle port, C/OpenMP)"},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML while the timed region runs."""
+
+    NAMES = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+             "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.stop_evt = [], set(), threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nvml = None
+
+    def _loop(self):
+        while not self.stop_evt.is_set():
+            try:
+                self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+                mask = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, bit in self.NAMES.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                break
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self.nvml:
+            self.t = threading.Thread(target=self._loop, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.nvml:
+            self.stop_evt.set()
+            self.t.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------ B200
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    import rdna2_ops
+    from rdna2_ops import _native as nat
+    from rdna2_ops import qlinear
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib = nat.library()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED + rank)
+
+    # Weight shard for this rank (config 2 weight per rank: weak scaling).
+    w = torch.randn((N, K), generator=gen, device=dev) * 0.02
+    wq, sw = qlinear.quantize_weight(w, rotation_block=ROT)
+    del w
+    bias = (torch.randn(N, generator=gen, device=dev) * 0.02).half()
+    xs = []
+    for s in range(args.sets):
+        x = torch.randn((M, K), generator=gen, device=dev)
+        idx = torch.randperm(K, generator=gen, device=dev)[: round(0.01 * K)]
+        x[:, idx] *= 20.0
+        xs.append(x.half())
+    # Distinct weight copies per set so no operand stays L2-resident across steps.
+    wqs = [wq] + [wq.clone() for _ in range(args.sets - 1)]
+    out = torch.empty((M, N), device=dev, dtype=torch.float16)
+    ws_bytes = lib.b2_quant_linear_workspace_bytes(M, K)
+    workspace = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        s = i % args.sets
+        st = lib.b2_quant_linear(nat.KIND_I8, xs[s].data_ptr(), nat.F16, M, K, K, ROT,
+                                 wqs[s].data_ptr(), K, N, sw.data_ptr(), N, bias.data_ptr(),
+                                 nat.F16, nat.EPI_SEPARATE, out.data_ptr(), nat.F16, N,
+                                 workspace.data_ptr(), ws_bytes, stream.cuda_stream)
+        if st:
+            nat.check(st, "b2_quant_linear")
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    nat.device_status(reset=True)
+
+    # ---- timed region: K fused-linear steps
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clocks:
+        t_wall = time.perf_counter()
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter() - t_wall
+    barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    value = world * 2.0 * M * N * K / (ms * 1e-3) / 1e12
+
+    # ---- dominant kernel alone (GEMM on pre-quantized activations), same stream
+    qa, sa = rdna2_ops.act_quant(xs[0], rotation_block=ROT)
+    qas = [qa] + [rdna2_ops.act_quant(xs[s], rotation_block=ROT)[0] for s in range(1, args.sets)]
+
+    def gemm(i):
+        s = i % args.sets
+        st = lib.b2_qgemm(nat.KIND_I8, qas[s].data_ptr(), K, wqs[s].data_ptr(), K, M, N, K,
+                          sa.data_ptr(), sw.data_ptr(), N, bias.data_ptr(), nat.F16,
+                          nat.EPI_SEPARATE, out.data_ptr(), nat.F16, N, stream.cuda_stream)
+        if st:
+            nat.check(st, "b2_qgemm")
+
+    for i in range(5):
+        gemm(i)
+    n_g = max(20, args.steps // 2)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(n_g):
+        gemm(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    gemm_ms = e0.elapsed_time(e1) / n_g
+    # prologue alone
+    e0.record(stream)
+    for i in range(n_g):
+        rdna2_ops.act_quant(xs[i % args.sets], rotation_block=ROT, out=qa, scale=sa)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    pro_ms = e0.elapsed_time(e1) / n_g
+
+    pk = peaks()
+    int8_peak = 2.0 * pk["bf16_tflops"]
+    achieved = 2.0 * M * N * K / (gemm_ms * 1e-3) / 1e12
+    traffic = None
+    prof = ROOT / "profiles" / "qgemm_i8_config2_traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+
+    # ---- end to end through the public API with host buffers
+    x_host = xs[0].cpu().pin_memory()
+    y_host = torch.empty((M, N), dtype=torch.float16).pin_memory()
+    w_scale = sw
+
+    def e2e_step():
+        xd = x_host.to(dev, non_blocking=True)
+        y = rdna2_ops.w8a8_linear(xd, wq, w_scale, bias, rotation_block=ROT,
+                                  out_dtype=torch.float16, workspace=workspace)
+        y_host.copy_(y, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    n_e = max(10, min(100, args.steps // 5))
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(n_e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / n_e
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = t.item()
+
+    # ---- all-gather that reassembles the column-parallel output (reported apart)
+    gather = None
+    if world > 1:
+        full = torch.empty((world, M, N), device=dev, dtype=torch.float16)
+        for _ in range(3):
+            dist.all_gather_into_tensor(full, out)
+        torch.cuda.synchronize()
+        barrier()
+        e0.record(stream)
+        for _ in range(10):
+            dist.all_gather_into_tensor(full, out)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        g_ms = e0.elapsed_time(e1) / 10
+        t = torch.tensor([g_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        g_ms = t.item()
+        gather = {"ms": round(g_ms, 4), "bytes_per_rank_received": (world - 1) * M * N * 2,
+                  "busbw_gbs": round((world - 1) * M * N * 2 / (g_ms * 1e-3) / 1e9, 1),
+                  "value_including_gather": round(world * 2.0 * M * N * K / ((ms + g_ms) * 1e-3) / 1e12, 2)}
+        del full
+
+    status = nat.device_status()
+    if rank != 0:
+        return
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_budget_s)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic",
+        "config": {"workload": "config2: W8A8 INT8 linear with block-128 Hadamard rotation, "
+                               "fp16 X[4096,3072] (1% outlier channels x20) -> fp16 Y[4096,12288]",
+                   "M": M, "N_per_rank": N, "K": K, "rotation_block": ROT,
+                   "parallelism": f"column-parallel N-shard x{world}" if world > 1 else "single GPU",
+                   "l2": f"inputs cycled over {args.sets} buffer sets "
+                         f"({args.sets * (M * K * 2 + N * K) / 2**20:.0f} MiB > 126 MB L2)"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
+                     "unit": "TOPS", "frac": round(achieved / int8_peak, 4), "traffic": traffic,
+                     "kernel": "qgemm_kernel<kind::i8,BN=256>",
+                     "peak_source": f"2 x bf16_tflops ({pk['source']}): kind::i8 issues at twice "
+                                    "the kind::f16 rate",
+                     "frac_of_nominal_4500": round(achieved / 4500.0, 4),
+                     "gemm_ms": round(gemm_ms, 5), "prologue_ms": round(pro_ms, 5),
+                     "prologue_gbs": round((M * K * 2 + M * K + M * 4) / (pro_ms * 1e-3) / 1e9, 1)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(world * 2.0 * M * N * K / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT,
+                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
+                "api": "rdna2_ops.w8a8_linear (C ABI b2_quant_linear), pinned host X in, Y out",
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+        "device_status": status,
+        "wall_s_timed": round(t_wall, 4),
+    }
+    if gather:
+        line["allgather"] = gather
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

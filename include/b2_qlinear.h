@@ -1,0 +1,107 @@
+/*
+ * b2_qlinear.h -- C ABI of the B200 (sm_100a) quantized-linear library
+ * (librdna2_b200.so).  Plain pointers, sizes and dtype codes; no framework
+ * types.  Conventions follow the reference's native ABI precedent
+ * (rdna2-ops/kernels.hip:283-319, `rdna2_group_norm_silu`):
+ *   - every entry point returns an int that is a cudaError_t value (0 = ok);
+ *   - work is enqueued asynchronously on the caller's stream (`void* stream`,
+ *     a cudaStream_t; NULL = legacy default stream);
+ *   - the caller owns and allocates every output and workspace buffer;
+ *     entry points never allocate device memory and never synchronize
+ *     (except b2_device_status, which is documented as synchronous);
+ *   - all device pointers belong to the current CUDA device.
+ *
+ * dtype codes:  0 = float32, 1 = float16, 2 = bfloat16, 3 = int32
+ * epilogue:     0 = separate  v = float(acc)*(sa*sb) [+ bias] in fp32, then cast
+ *                               (rdna2_ops/int8_gemm.py:53-63, rounding="separate")
+ *               1 = fma       v = fma(float(acc), sa*sb, bias)  (rounding="fused")
+ *               2 = kitchen   y = cast(float(acc)*(sa*sb)); y = cast(y + cast(bias))
+ *                               (production/MOSS_RDNA2_INT8/backend.py:128-143)
+ *               3 = none      raw int32 accumulator (out_dtype must be 3)
+ * kind:         0 = int8 x int8 -> int32 (tcgen05 kind::i8)
+ *               1 = e4m3 x e4m3 -> fp32  (tcgen05 kind::f8f6f4)
+ *               2 = bf16 x bf16 -> fp32  (tcgen05 kind::f16)
+ */
+#ifndef B2_QLINEAR_H_
+#define B2_QLINEAR_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Library ABI version (increments on any signature change). */
+int b2_version(void);
+
+/* Human-readable text for a status code returned by any entry point. */
+const char* b2_error_string(int status);
+
+/* Number of SMs the persistent kernels size their grid to on the current
+ * device. */
+int b2_sm_count(void);
+
+/* SYNCHRONOUS: read (and if reset != 0 clear) the device status word that a
+ * kernel sets when one of its bounded waits gives up (0 = no failure; else
+ * 0x100 | site).  Call after synchronizing the stream. */
+int b2_device_status(int* status, int reset);
+
+/* Activation prologue: optional block-Hadamard rotation, per-row absmax,
+ * round-to-nearest-even quantization.
+ *   x      [M,K] of x_dtype (0/1/2), row stride ldx elements
+ *   block  0 or 1 = no rotation; else a power of two dividing K (<= 4096)
+ *   quant  0 = int8 (scale = absmax/127, codes in [-127,127]);
+ *          1 = e4m3 (scale = absmax/448, saturating)
+ *   q      [M,K] 1-byte codes, row stride ldq bytes (columns >= K untouched)
+ *   scale  [M] fp32
+ * Replaces Kitchen's _rotate_activation + quantize_int8_rowwise at
+ * production/MOSS_RDNA2_INT8/backend.py:112-122 and rdna2_ops/int8_gemm.py:249-255,
+ * and the row quantizer rdna2_ops/fp8_weight_gemm_v06.py:76-92. */
+int b2_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
+                 int quant, void* q, int64_t ldq, float* scale, void* stream);
+
+/* Quantized GEMM with fused epilogue: out[m,n] = epi(sum_k a[m,k]*b[n,k]).
+ *   a       [M,K] K-major, row stride lda elements, 16-byte aligned base,
+ *           lda*elem a multiple of 16
+ *   b       [N,K] K-major (the weight as stored), same alignment rules
+ *   a_scale [M] fp32 (NULL only with epilogue 3)
+ *   b_scale [N] fp32 or a single fp32 when b_scale_count == 1
+ *   bias    [N] of bias_dtype (0/1/2) or NULL
+ *   out     [M,N] of out_dtype, row stride ldc elements
+ * Replaces rdna2_ops/int8_gemm.py:152-214 (int8_matmul, int8_gemm_dequant,
+ * kernel _int8_dot_dequant at :19-67).  Requires K <= 131071 for kind 0. */
+int b2_qgemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M,
+             int64_t N, int64_t K, const float* a_scale, const float* b_scale,
+             int64_t b_scale_count, const void* bias, int bias_dtype, int epilogue, void* out,
+             int out_dtype, int64_t ldc, void* stream);
+
+/* Strided -> K-major copy used for operand views the TMA cannot read
+ * directly (odd strides, transposed [K,N] weights):
+ *   dst[r*ldd + c] = src[r*s_row + c*s_col] for c < cols, 0 for cols <= c < ldd.
+ * elem_bytes 1 or 2; strides in elements.  Serves the stride-aware contract of
+ * rdna2_ops/int8_gemm.py:39-40 for layouts outside the fast path. */
+int b2_repack(const void* src, int elem_bytes, int64_t rows, int64_t cols, int64_t s_row,
+              int64_t s_col, void* dst, int64_t ldd, void* stream);
+
+/* Workspace bytes b2_quant_linear needs for an [M,K] activation. */
+size_t b2_quant_linear_workspace_bytes(int64_t M, int64_t K);
+
+/* Fused quantized linear: act_quant (rotation + per-token quantization of x)
+ * followed by b2_qgemm against a pre-quantized weight.
+ *   kind 0: W8A8 INT8 (w int8 [N,K]); kind 1: FP8 (w e4m3 [N,K])
+ *   w_scale [N] fp32 or one fp32 (w_scale_count 1)
+ *   workspace >= b2_quant_linear_workspace_bytes(M, K), 256-byte aligned
+ * Replaces production/MOSS_RDNA2_INT8/backend.py:71-145 (int8_linear) and
+ * rdna2_ops/int8_gemm.py:231-263 (moss_int8_gemm_candidate's candidate). */
+int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                    int block, const void* w, int64_t ldw, int64_t N, const float* w_scale,
+                    int64_t w_scale_count, const void* bias, int bias_dtype, int epilogue,
+                    void* out, int out_dtype, int64_t ldc, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2_QLINEAR_H_ */

@@ -1,0 +1,40 @@
+// Host-side declarations shared by the CUDA translation units of the library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace b2 {
+
+struct GemmParams {
+  int M, N, K;
+  int tiles_m, tiles_n, num_kb;
+  const float* sa;     // [M] per-row scale; nullptr for raw accumulators
+  const float* sb;     // [N] per-channel scale, or [1] when sb_scalar
+  int sb_scalar;
+  const void* bias;    // [N] or nullptr
+  int bias_dtype;
+  void* out;
+  int out_dtype;
+  int64_t ldc;         // output row stride in elements
+  int epilogue;
+  int vec_ok;          // output rows 16-byte aligned: vector stores allowed
+};
+
+int device_sm_count();
+
+// a: [M,K] K-major with row stride lda (elements); b: [N,K] K-major, ldb.
+// Both base pointers 16-byte aligned, lda/ldb * element size multiples of 16.
+cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
+                      GemmParams p, int max_ctas, cudaStream_t stream);
+
+// Per-row rotate + quantize (quant 0 = int8 /127, 1 = e4m3 /448).
+cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                          int block, int quant, void* q, int64_t ldq, float* scale,
+                          cudaStream_t stream);
+
+// dst[r, c] = src[r*s_row + c*s_col] for c < cols, 0 for cols <= c < ldd.
+cudaError_t run_repack(const void* src, int elem_bytes, int64_t rows, int64_t cols, int64_t s_row,
+                       int64_t s_col, void* dst, int64_t ldd, cudaStream_t stream);
+
+}  // namespace b2

@@ -1,0 +1,149 @@
+// C ABI of librdna2_b200.so: argument validation and dispatch to the kernels.
+// Every check here mirrors a Python-side check of the reference
+// (rdna2_ops/int8_gemm.py:131-178) so a bad call fails with a status code
+// before anything is launched.
+#include <cstdint>
+
+#include "../../include/b2_qlinear.h"
+#include "b2_common.cuh"
+#include "b2_internal.h"
+
+namespace {
+
+constexpr int kAbiVersion = 1;
+
+inline bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+inline int fail() { return static_cast<int>(cudaErrorInvalidValue); }
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+bool valid_block(int block, int64_t K) {
+  if (block <= 1) return true;
+  if (block & (block - 1)) return false;
+  if (block > 4096) return false;
+  return K % block == 0;
+}
+
+int elem_bytes(int kind) { return kind == b2::kKindBF16 ? 2 : 1; }
+
+int check_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N,
+               int64_t K, const float* a_scale, const float* b_scale, int64_t b_scale_count,
+               const void* bias, int bias_dtype, int epilogue, const void* out, int out_dtype,
+               int64_t ldc) {
+  if (kind < 0 || kind > 2) return fail();
+  if (M < 0 || N < 0 || K < 1 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail();
+  if (kind == b2::kKindI8 && K > 131071) return fail();  // INT32 accumulator bound
+  if (M == 0 || N == 0) return 0;
+  const int eb = elem_bytes(kind);
+  if (!a || !b || !out) return fail();
+  if (!aligned16(a) || !aligned16(b)) return fail();
+  if (lda < K || ldb < K || (lda * eb) % 16 || (ldb * eb) % 16) return fail();
+  if (ldc < N) return fail();
+  if (epilogue < 0 || epilogue > 3) return fail();
+  if (epilogue == b2::kEpiNone) {
+    if (out_dtype != b2::kI32 || kind != b2::kKindI8) return fail();
+  } else {
+    if (out_dtype < 0 || out_dtype > 2) return fail();
+    if (!a_scale || !b_scale) return fail();
+    if (b_scale_count != 1 && b_scale_count != N) return fail();
+    if (bias && (bias_dtype < 0 || bias_dtype > 2)) return fail();
+  }
+  return 0;
+}
+
+b2::GemmParams make_params(int64_t M, int64_t N, int64_t K, const float* a_scale,
+                           const float* b_scale, int64_t b_scale_count, const void* bias,
+                           int bias_dtype, int epilogue, void* out, int out_dtype, int64_t ldc) {
+  b2::GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  const bool raw = epilogue == b2::kEpiNone;
+  p.sa = raw ? nullptr : a_scale;
+  p.sb = raw ? nullptr : b_scale;
+  p.sb_scalar = (!raw && b_scale_count == 1) ? 1 : 0;
+  p.bias = raw ? nullptr : bias;
+  p.bias_dtype = bias_dtype;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.ldc = ldc;
+  p.epilogue = epilogue;
+  const int ob = (out_dtype == b2::kF16 || out_dtype == b2::kBF16) ? 2 : 4;
+  p.vec_ok = aligned16(out) && ((ldc * ob) % 16 == 0);
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2_version(void) { return kAbiVersion; }
+
+const char* b2_error_string(int status) { return cudaGetErrorString(static_cast<cudaError_t>(status)); }
+
+int b2_sm_count(void) { return b2::device_sm_count(); }
+
+int b2_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block, int quant,
+                 void* q, int64_t ldq, float* scale, void* stream) {
+  if (M < 0 || K < 1 || M > INT32_MAX || K > 16384) return fail();
+  if (x_dtype < 0 || x_dtype > 2 || quant < 0 || quant > 1) return fail();
+  if (!valid_block(block, K)) return fail();
+  if (M == 0) return 0;
+  if (!x || !q || !scale || ldx < K || ldq < K) return fail();
+  return static_cast<int>(b2::run_act_quant(x, x_dtype, M, K, ldx, block, quant, q, ldq, scale,
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+int b2_qgemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N,
+             int64_t K, const float* a_scale, const float* b_scale, int64_t b_scale_count,
+             const void* bias, int bias_dtype, int epilogue, void* out, int out_dtype, int64_t ldc,
+             void* stream) {
+  int st = check_gemm(kind, a, lda, b, ldb, M, N, K, a_scale, b_scale, b_scale_count, bias,
+                      bias_dtype, epilogue, out, out_dtype, ldc);
+  if (st != 0 || M == 0 || N == 0) return st;
+  b2::GemmParams p = make_params(M, N, K, a_scale, b_scale, b_scale_count, bias, bias_dtype,
+                                 epilogue, out, out_dtype, ldc);
+  return static_cast<int>(b2::run_qgemm(kind, a, lda, b, ldb, p, 0, static_cast<cudaStream_t>(stream)));
+}
+
+int b2_repack(const void* src, int elem_bytes_, int64_t rows, int64_t cols, int64_t s_row,
+              int64_t s_col, void* dst, int64_t ldd, void* stream) {
+  if (rows < 0 || cols < 0 || ldd < cols || (elem_bytes_ != 1 && elem_bytes_ != 2)) return fail();
+  if (rows == 0 || ldd == 0) return 0;
+  if (!src || !dst) return fail();
+  return static_cast<int>(b2::run_repack(src, elem_bytes_, rows, cols, s_row, s_col, dst, ldd,
+                                         static_cast<cudaStream_t>(stream)));
+}
+
+size_t b2_quant_linear_workspace_bytes(int64_t M, int64_t K) {
+  if (M <= 0 || K <= 0) return 0;
+  return static_cast<size_t>(round_up(M * round_up(K, 16), 256) + round_up(M * 4, 256));
+}
+
+int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
+                    const void* w, int64_t ldw, int64_t N, const float* w_scale,
+                    int64_t w_scale_count, const void* bias, int bias_dtype, int epilogue, void* out,
+                    int out_dtype, int64_t ldc, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  if (kind != b2::kKindI8 && kind != b2::kKindE4M3) return fail();
+  if (epilogue == b2::kEpiNone) return fail();
+  if (M < 0 || K < 1 || K > 16384 || x_dtype < 0 || x_dtype > 2 || !valid_block(block, K)) return fail();
+  const int64_t ldq = round_up(K, 16);
+  // Validate the GEMM half with the staging buffer standing in for `a`.
+  int st = check_gemm(kind, workspace, ldq, w, ldw, M, N, K, w_scale, w_scale, w_scale_count,
+                      bias, bias_dtype, epilogue, out, out_dtype, ldc);
+  if (st != 0 || M == 0 || N == 0) return st;
+  if (!x || ldx < K) return fail();
+  if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail();
+  if (workspace_bytes < b2_quant_linear_workspace_bytes(M, K)) return fail();
+  uint8_t* q = static_cast<uint8_t*>(workspace);
+  float* sa = reinterpret_cast<float*>(q + round_up(M * ldq, 256));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = b2::run_act_quant(x, x_dtype, M, K, ldx, block, kind == b2::kKindE4M3 ? 1 : 0, q,
+                                    ldq, sa, s);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  b2::GemmParams p = make_params(M, N, K, sa, w_scale, w_scale_count, bias, bias_dtype, epilogue,
+                                 out, out_dtype, ldc);
+  return static_cast<int>(b2::run_qgemm(kind, q, ldq, w, ldw, p, 0, s));
+}
+
+}  // extern "C"

@@ -1,0 +1,249 @@
+"""GPU parity of the W8A8 / FP8 hot path against the CPU oracle and the
+reference's golden vectors.  Integer work (codes, INT32 accumulators) is
+bit-exact; fp32/fp16/bf16 outputs of the INT8 path are bit-exact too (the
+epilogue reproduces the reference rounding order).  FP8 outputs: within the
+stated accumulation tolerance."""
+import numpy as np
+import pytest
+
+import oracle
+from conftest import outlier_activations
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import rdna2_ops  # noqa: E402
+from rdna2_ops import _native as nat  # noqa: E402
+from rdna2_ops import qlinear  # noqa: E402
+
+ODT = {torch.float32: oracle.F32, torch.float16: oracle.F16, torch.bfloat16: oracle.BF16}
+EPI = {"separate": oracle.EPI_SEPARATE, "fused": oracle.EPI_FMA, "kitchen": oracle.EPI_KITCHEN}
+
+
+def cuda(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def bits(t):
+    """Tensor -> numpy storage bits matching the oracle conventions."""
+    t = t.detach().cpu()
+    if t.dtype == torch.float32:
+        return t.numpy()
+    return t.view(torch.int16).numpy().view(np.uint16)
+
+
+def same_bits(t, ref):
+    got = bits(t)
+    if got.dtype == np.float32:
+        return np.array_equal(got.view(np.uint32), np.asarray(ref, np.float32).view(np.uint32))
+    return np.array_equal(got, ref)
+
+
+def x_tensor(x32, dtype):
+    return torch.from_numpy(x32).to(dtype).cuda()
+
+
+def x_bits(xt):
+    return bits(xt)
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _device_status_clean():
+    nat.device_status(reset=True)
+    yield
+    assert nat.device_status() == 0, "a kernel's bounded wait gave up"
+
+
+# ------------------------------------------------------- golden: INT8 GEMM
+@pytest.mark.parametrize("key", ["weight_nk_vector", "weight_nk_scalar", "rhs_kn_vector",
+                                 "rhs_kn_scalar"])
+def test_int8_known_answer(golden, key):
+    """bench_int8_gemm.py:181-203 on the GPU: offset+padded A view, weight.T view
+    and contiguous [K,N] B, INT32 exact, FP32 dequant bitwise."""
+    g = golden("int8_known_answer.npz")
+    a = cuda(g[key + "_a_store"])[1:38, 1:80]
+    w = cuda(g[key + "_w"])
+    b = w.T if key.startswith("weight_nk") else w.T.contiguous()
+    acc = rdna2_ops.int8_matmul(a, b)
+    assert acc.dtype == torch.int32 and np.array_equal(acc.cpu().numpy(), g[key + "_acc"])
+    out = rdna2_ops.int8_gemm_dequant(a, b, cuda(g[key + "_sa"]), cuda(g[key + "_sb"]),
+                                      cuda(g[key + "_bias"]))
+    assert same_bits(out, g[key + "_ref"])
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (1, 16, 16), (37, 53, 79), (129, 257, 33),
+                                   (128, 256, 128), (300, 200, 1000), (513, 640, 3072),
+                                   (64, 96, 131071 // 8)])
+def test_int8_matmul_exact(m, n, k):
+    rng = np.random.default_rng(m * 7 + n * 3 + k)
+    a = rng.integers(-128, 128, (m, k), dtype=np.int8)
+    w = rng.integers(-128, 128, (n, k), dtype=np.int8)
+    ref = oracle.gemm_s8(a, w)
+    got = rdna2_ops.int8_matmul(cuda(a), cuda(w).T)
+    assert np.array_equal(got.cpu().numpy(), ref)
+    got2 = rdna2_ops.int8_matmul(cuda(a), cuda(w).T.contiguous())      # [K,N] layout
+    assert np.array_equal(got2.cpu().numpy(), ref)
+
+
+def test_int8_accumulator_extremes():
+    k = 4096
+    a = np.full((130, k), -128, np.int8)
+    w = np.full((140, k), -128, np.int8)
+    w[1::2] = 127
+    got = rdna2_ops.int8_matmul(cuda(a), cuda(w).T).cpu().numpy()
+    assert np.array_equal(got, oracle.gemm_s8(a, w))
+
+
+@pytest.mark.parametrize("rounding", ["separate", "fused"])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("scalar", [False, True])
+def test_int8_gemm_dequant_epilogues(rounding, out_dtype, scalar):
+    rng = np.random.default_rng(11)
+    m, n, k = 200, 264, 512
+    a = rng.integers(-127, 128, (m, k), dtype=np.int8)
+    w = rng.integers(-127, 128, (n, k), dtype=np.int8)
+    sa = (rng.random(m) * 0.02 + 0.001).astype(np.float32)
+    sb = (rng.random(1 if scalar else n) * 0.02 + 0.001).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    acc = oracle.gemm_s8(a, w)
+    ref = oracle.epilogue_s32(acc, sa, sb, bias, oracle.F32, EPI[rounding], ODT[out_dtype])
+    out = rdna2_ops.int8_gemm_dequant(cuda(a), cuda(w).T, cuda(sa), cuda(sb), cuda(bias),
+                                      rounding=rounding, out_dtype=out_dtype)
+    assert same_bits(out, ref)
+
+
+# ----------------------------------------------------- prologue (act_quant)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("k,block", [(3072, 128), (3072, None), (3072, 256), (3072, 1024),
+                                     (384, 128), (4096, 128), (5120, 128), (12288, 128),
+                                     (8192, 2048), (16384, 256), (80, 16), (24, None)])
+def test_act_quant_bit_exact(dtype, k, block):
+    rng = np.random.default_rng(k + (block or 0))
+    m = 67
+    x32 = outlier_activations(rng, m, k)
+    x32[3] = 0.0                                   # all-zero row -> scale 1, codes 0
+    xt = x_tensor(x32, dtype)
+    q, s = rdna2_ops.act_quant(xt, rotation_block=block)
+    ref_q, ref_s = oracle.act_quant_int8(x_bits(xt), ODT[dtype], block or 0)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), ref_s.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), ref_q)
+
+
+def test_act_quant_e4m3_bit_exact():
+    rng = np.random.default_rng(5)
+    x32 = outlier_activations(rng, 33, 5120)
+    xt = x_tensor(x32, torch.bfloat16)
+    q, s = rdna2_ops.act_quant(xt, quant="e4m3")
+    ref_q, ref_s = oracle.quant_rows_e4m3(oracle.rotate_rows(x_bits(xt), oracle.BF16, 0))
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), ref_s.view(np.uint32))
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), ref_q)
+
+
+def test_act_quant_strided_rows():
+    rng = np.random.default_rng(6)
+    big = outlier_activations(rng, 40, 1000)
+    xt = x_tensor(big, torch.float16)[:, 8:8 + 768]   # row stride 1000, offset 8
+    q, s = rdna2_ops.act_quant(xt, rotation_block=256)
+    ref_q, ref_s = oracle.act_quant_int8(x_bits(xt), oracle.F16, 256)
+    assert np.array_equal(q.cpu().numpy(), ref_q)
+    assert np.array_equal(s.cpu().numpy(), ref_s)
+
+
+# ------------------------------------------------------ fused W8A8 linear
+def _weights(rng, n, k, block):
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    wq, sw = oracle.quant_rows_int8(oracle.rotate_rows(w, oracle.F32, block or 0))
+    return w, wq, sw
+
+
+@pytest.mark.parametrize("m,n,k,block", [(1, 64, 128, 128), (37, 53, 96, None),
+                                         (128, 256, 3072, 128), (200, 384, 512, 256),
+                                         (333, 4000, 1024, 128)])
+@pytest.mark.parametrize("epilogue", ["separate", "kitchen", "fused"])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_w8a8_linear_bit_exact(m, n, k, block, epilogue, out_dtype):
+    rng = np.random.default_rng(m + n + k)
+    x32 = outlier_activations(rng, m, k)
+    _, wq, sw = _weights(rng, n, k, block)
+    bias = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    xt = x_tensor(x32, torch.float16)
+    bias_t = torch.from_numpy(bias).to(torch.float16).cuda()
+    y = rdna2_ops.w8a8_linear(xt, cuda(wq), cuda(sw), bias_t, rotation_block=block,
+                              out_dtype=out_dtype, epilogue=epilogue)
+    ref = oracle.w8a8_linear(x_bits(xt), oracle.F16, block or 0, wq, sw, bits(bias_t),
+                             oracle.F16, EPI[epilogue], ODT[out_dtype])
+    assert same_bits(y, ref)
+
+
+def test_quantize_weight_folds_rotation_bit_exact():
+    rng = np.random.default_rng(9)
+    w = (rng.standard_normal((300, 3072)) * 0.02).astype(np.float32)
+    q, s = qlinear.quantize_weight(cuda(w), rotation_block=128)
+    rq, rs = oracle.quant_rows_int8(oracle.rotate_rows(w, oracle.F32, 128))
+    assert np.array_equal(q.cpu().numpy(), rq) and np.array_equal(s.cpu().numpy(), rs)
+
+
+def test_config1_full_size_bit_exact():
+    """X fp16 [1024,3072] with 1% outlier channels, W int8
+    [3072,3072] per-channel, fp16 bias, fp16 out, no rotation."""
+    rng = np.random.default_rng(20261106)
+    m, n, k = 1024, 3072, 3072
+    x32 = outlier_activations(rng, m, k)
+    _, wq, sw = _weights(rng, n, k, None)
+    bias_t = torch.from_numpy((rng.standard_normal(n) * 0.02).astype(np.float32)).half().cuda()
+    xt = x_tensor(x32, torch.float16)
+    y = rdna2_ops.w8a8_linear(xt, cuda(wq), cuda(sw), bias_t, out_dtype=torch.float16)
+    ref = oracle.w8a8_linear(x_bits(xt), oracle.F16, 0, wq, sw, bits(bias_t), oracle.F16,
+                             oracle.EPI_SEPARATE, oracle.F16)
+    assert same_bits(y, ref)
+
+
+def test_config2_full_size_sampled_and_deterministic():
+    """BASELINE config 2 at full size (4096 x 12288 x 3072, rotation 128): codes
+    and scales bit-exact for every row; outputs bit-exact on a 128x160 sample
+    checked by the oracle; two runs bitwise identical."""
+    rng = np.random.default_rng(20261105)
+    m, n, k = 4096, 12288, 3072
+    xt = x_tensor(outlier_activations(rng, m, k), torch.float16)
+    wt = torch.from_numpy((rng.standard_normal((n, k)) * 0.02).astype(np.float32)).cuda()
+    wq, sw = qlinear.quantize_weight(wt, rotation_block=128)
+    y1 = rdna2_ops.w8a8_linear(xt, wq, sw, rotation_block=128, out_dtype=torch.float16)
+    y2 = rdna2_ops.w8a8_linear(xt, wq, sw, rotation_block=128, out_dtype=torch.float16)
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
+    q, s = rdna2_ops.act_quant(xt, rotation_block=128)
+    rq, rs = oracle.act_quant_int8(bits(xt), oracle.F16, 128)
+    assert np.array_equal(q.cpu().numpy(), rq) and np.array_equal(s.cpu().numpy(), rs)
+    rows = np.sort(rng.choice(m, 128, replace=False))
+    cols = np.sort(rng.choice(n, 160, replace=False))
+    wq_np, sw_np = wq.cpu().numpy(), sw.cpu().numpy()
+    acc = oracle.gemm_s8(rq[rows], wq_np[cols])
+    ref = oracle.epilogue_s32(acc, rs[rows], sw_np[cols], out_dtype=oracle.F16)
+    got = bits(y1)[np.ix_(rows, cols)]
+    assert np.array_equal(got, ref)
+
+
+# -------------------------------------------------------------------- FP8
+@pytest.mark.parametrize("m", [1, 2048])
+def test_fp8_linear_matches_fp64_oracle(m):
+    """BASELINE config 4 (A bf16 -> e4m3 per token, W e4m3 per channel, bf16
+    out; K = N = 5120, plus the M = 1 decode shape).  Codes bit-exact; outputs
+    within 1 bf16 ulp plus 2^-12 of the summed |products| (fp32 accumulation
+    order)."""
+    rng = np.random.default_rng(20261108 + m)
+    n = k = 5120
+    xt = x_tensor(rng.standard_normal((m, k)).astype(np.float32), torch.bfloat16)
+    w = torch.from_numpy((rng.standard_normal((n, k)) * 0.02).astype(np.float32)).cuda()
+    wq, sw = qlinear.quantize_weight(w, quant="e4m3")
+    y = rdna2_ops.fp8_linear(xt, wq, sw, out_dtype=torch.bfloat16)
+    aq, sa = oracle.quant_rows_e4m3(oracle.decode(bits(xt), oracle.BF16))
+    wq_np = wq.view(torch.uint8).cpu().numpy()
+    rows = np.arange(m) if m < 64 else np.sort(rng.choice(m, 64, replace=False))
+    acc = oracle.gemm_e4m3_f64(aq[rows], wq_np)
+    absacc = oracle.gemm_f32_f64(np.abs(oracle.decode_e4m3(aq[rows])),
+                                 np.abs(oracle.decode_e4m3(wq_np)))
+    swn = sw.cpu().numpy()
+    ref = acc * (sa[rows, None].astype(np.float64) * swn[None, :])
+    got = oracle.decode(bits(y)[rows], oracle.BF16).astype(np.float64)
+    ulp = np.maximum(np.abs(ref), 1e-30) * 2.0 ** -8
+    tol = ulp + 2.0 ** -12 * absacc * (sa[rows, None] * swn[None, :])
+    assert np.all(np.abs(got - ref) <= tol)
