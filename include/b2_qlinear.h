@@ -42,6 +42,13 @@ const char* b2_error_string(int status);
  * device. */
 int b2_sm_count(void);
 
+/* Process-wide GEMM kernel selection: 0 = automatic (2-CTA pair kernel when
+ * M > 128, else single-CTA), 1 = single-CTA kernel only, 2 = pair kernel
+ * only.  A tuning and verification knob; results are identical either way.
+ * No reference counterpart (the reference exposes tile keywords instead,
+ * rdna2_ops/int8_gemm.py:195-214). */
+int b2_set_gemm_path(int path);
+
 /* SYNCHRONOUS: read (and if reset != 0 clear) the device status word that a
  * kernel sets when one of its bounded waits gives up (0 = no failure; else
  * 0x100 | site).  Call after synchronizing the stream. */

@@ -28,6 +28,9 @@ int device_sm_count();
 cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
                       GemmParams p, int max_ctas, cudaStream_t stream);
 
+// 0 = automatic, 1 = single-CTA kernel only, 2 = 2-CTA pair kernel only.
+void set_gemm_path(int path);
+
 // Per-row rotate + quantize (quant 0 = int8 /127, 1 = e4m3 /448).
 cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                           int block, int quant, void* q, int64_t ldq, float* scale,

@@ -4,16 +4,25 @@
 // K-major (B is the weight in its stored [N,K] layout, i.e. the reference's
 // `weight.T` view of rdna2_ops/int8_gemm.py:39-40 without a copy).
 //
-// Design (one persistent CTA per SM, 192 threads):
-//   warp 0      TMA producer: 128B-swizzled A/B k-blocks into a STAGES-deep
-//               shared-memory ring (plain tile loads, never multicast).
-//   warp 1      TMEM owner + single-thread tcgen05.mma issuer (kind::i8 for
-//               W8A8, kind::f8f6f4 for e4m3, kind::f16 for bf16), 128 x BN
-//               tiles, 4 MMAs (32 bytes of K each) per k-block.
-//   warps 2..5  epilogue: tcgen05.ld of the 128 x BN accumulator (double
-//               buffered in TMEM so tile t+1's MMAs overlap tile t's
-//               epilogue), per-token x per-channel scale, bias and cast, then
-//               direct 16-byte global stores.
+// Two persistent, warp-specialized kernels (192 threads per CTA, one CTA per
+// SM):
+//   qgemm_pair_kernel  2-CTA cluster; the leader CTA issues tcgen05.mma
+//                      .cta_group::2 on a 256 x BN tile whose A rows and B
+//                      columns are split across the two CTAs' shared memory,
+//                      so each SM reads half the B operand per MMA and the
+//                      ring holds 6-7 stages.  Used whenever M > 128.
+//   qgemm_kernel       single CTA, 128 x BN tile; small-M problems.
+// Roles in both:
+//   warp 0      TMA producer into a STAGES-deep ring of 128B-swizzled k-blocks
+//               (plain tile loads; pair loads count bytes on the leader's
+//               barrier; never multicast).
+//   warp 1      TMEM owner + single-thread MMA issuer (kind::i8 for W8A8,
+//               kind::f8f6f4 for e4m3, kind::f16 for bf16), 4 MMAs of 32 bytes
+//               of K per k-block; commits free ring slots and publish finished
+//               accumulators.
+//   warps 2..5  epilogue: double-buffered TMEM accumulators let tile t+1's
+//               MMAs overlap tile t's epilogue; tcgen05.ld ping-pong buffers,
+//               per-token x per-channel scale, bias and cast, 16-byte stores.
 //
 // Epilogue rounding follows the reference exactly:
 //   separate  float(acc)*(sa*sb) then + bias in fp32, two roundings
@@ -30,20 +39,29 @@
 
 namespace b2 {
 
-template <int BN, int STAGES>
-struct GemmSmem {
-  static constexpr int kABytes = 128 * 128;
-  static constexpr int kBBytes = BN * 128;
+constexpr int kEpiWarps = 4;
+
+__host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
+  return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
+}
+
+// Shared-memory plan: A ring, B ring, per-warp epilogue scale/bias, barriers.
+template <int A_ROWS, int B_ROWS, int BN, int STAGES>
+struct Smem {
+  static constexpr int kABytes = A_ROWS * 128;
+  static constexpr int kBBytes = B_ROWS * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = STAGES * kABytes;
-  static constexpr int kOffBar = STAGES * kStageBytes;
+  static constexpr int kOffEpi = STAGES * kStageBytes;
+  static constexpr int kOffBar = kOffEpi + kEpiWarps * 2 * BN * 4;
   static constexpr int kNumBars = 2 * STAGES + 4;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
-  static constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64
-                                        : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  static constexpr uint32_t kTmemCols = tmem_cols_for(2 * BN);
+  static_assert(kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle atoms need 1 KiB alignment");
+  static_assert(kAlloc <= 232448, "shared memory budget");
 };
 
 template <int OUT>
@@ -83,24 +101,29 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int out) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// One thread, one output row, 32 consecutive columns starting at n.
+// One thread, one output row, 32 consecutive columns starting at n; the
+// chunk's per-channel scales and bias come from this warp's shared staging.
 template <int KIND, int MODE, int OUT>
 __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t (&r)[32], int row,
-                                            int n, float sa, float sb_lane, float bias_lane,
-                                            bool has_bias) {
-  // All 32 lanes run the shuffles; rows past M only skip the stores.
+                                            int n, float sa, const float* csb, const float* cbias) {
+  if (row >= p.M) return;
+  const bool hb = p.bias != nullptr;
   float v[32];
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const float sbj = p.sb_scalar ? sb_lane : __shfl_sync(0xffffffffu, sb_lane, j);
-    const float bj = __shfl_sync(0xffffffffu, bias_lane, j);
-    if constexpr (MODE == kEpiNone) {
-      v[j] = __uint_as_float(r[j]);
-    } else {
-      v[j] = epi_value<KIND, MODE, OUT>(r[j], sa, sbj, bj, has_bias);
+  for (int j = 0; j < 32; j += 4) {
+    const float4 s4 = *reinterpret_cast<const float4*>(csb + j);
+    const float4 b4 = *reinterpret_cast<const float4*>(cbias + j);
+    const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
+    const float bv[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (MODE == kEpiNone) {
+        v[j + i] = __uint_as_float(r[j + i]);
+      } else {
+        v[j + i] = epi_value<KIND, MODE, OUT>(r[j + i], sa, sv[i], bv[i], hb);
+      }
     }
   }
-  if (row >= p.M) return;
   const int64_t base = static_cast<int64_t>(row) * p.ldc + n;
   if (p.vec_ok && n + 32 <= p.N) {
     if constexpr (OUT == kF32 || OUT == kI32) {
@@ -135,28 +158,81 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
 
 template <int KIND>
 __device__ __forceinline__ void store_dispatch(const GemmParams& p, const uint32_t (&r)[32], int row,
-                                               int n, float sa, float sb_lane, float bias_lane) {
-  const bool hb = p.bias != nullptr;
+                                               int n, float sa, const float* csb, const float* cb) {
   switch (p.epilogue * 4 + p.out_dtype) {
-    case kEpiNone * 4 + kI32: store_chunk<KIND, kEpiNone, kI32>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
-    case kEpiSeparate * 4 + kF32: store_chunk<KIND, kEpiSeparate, kF32>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
-    case kEpiSeparate * 4 + kF16: store_chunk<KIND, kEpiSeparate, kF16>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
-    case kEpiSeparate * 4 + kBF16: store_chunk<KIND, kEpiSeparate, kBF16>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
-    case kEpiFma * 4 + kF32: store_chunk<KIND, kEpiFma, kF32>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
-    case kEpiFma * 4 + kF16: store_chunk<KIND, kEpiFma, kF16>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
-    case kEpiFma * 4 + kBF16: store_chunk<KIND, kEpiFma, kBF16>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
-    case kEpiKitchen * 4 + kF32: store_chunk<KIND, kEpiKitchen, kF32>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
-    case kEpiKitchen * 4 + kF16: store_chunk<KIND, kEpiKitchen, kF16>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
-    case kEpiKitchen * 4 + kBF16: store_chunk<KIND, kEpiKitchen, kBF16>(p, r, row, n, sa, sb_lane, bias_lane, hb); break;
+    case kEpiNone * 4 + kI32: store_chunk<KIND, kEpiNone, kI32>(p, r, row, n, sa, csb, cb); break;
+    case kEpiSeparate * 4 + kF32: store_chunk<KIND, kEpiSeparate, kF32>(p, r, row, n, sa, csb, cb); break;
+    case kEpiSeparate * 4 + kF16: store_chunk<KIND, kEpiSeparate, kF16>(p, r, row, n, sa, csb, cb); break;
+    case kEpiSeparate * 4 + kBF16: store_chunk<KIND, kEpiSeparate, kBF16>(p, r, row, n, sa, csb, cb); break;
+    case kEpiFma * 4 + kF32: store_chunk<KIND, kEpiFma, kF32>(p, r, row, n, sa, csb, cb); break;
+    case kEpiFma * 4 + kF16: store_chunk<KIND, kEpiFma, kF16>(p, r, row, n, sa, csb, cb); break;
+    case kEpiFma * 4 + kBF16: store_chunk<KIND, kEpiFma, kBF16>(p, r, row, n, sa, csb, cb); break;
+    case kEpiKitchen * 4 + kF32: store_chunk<KIND, kEpiKitchen, kF32>(p, r, row, n, sa, csb, cb); break;
+    case kEpiKitchen * 4 + kF16: store_chunk<KIND, kEpiKitchen, kF16>(p, r, row, n, sa, csb, cb); break;
+    case kEpiKitchen * 4 + kBF16: store_chunk<KIND, kEpiKitchen, kBF16>(p, r, row, n, sa, csb, cb); break;
     default: break;
   }
 }
 
+// Epilogue of one accumulator tile by one warp (32 rows x BN columns).
+// `release` runs once every TMEM read of the tile has completed.
+template <int KIND, int BN, typename Release>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t taddr, int row, int n0,
+                                              int lane, float* wsb, Release release) {
+  constexpr int NC = BN / 32;
+  static_assert(NC % 2 == 0, "ping-pong over chunk pairs");
+  float* wbias = wsb + BN;
+  // Stage this tile's per-channel scale and bias in the warp's own slice.
+  __syncwarp();
+  const float sb0 = (p.sb != nullptr && p.sb_scalar) ? p.sb[0] : 0.0f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int n = n0 + c * 32 + lane;
+    float sb = sb0, b = 0.0f;
+    if (n < p.N) {
+      if (p.sb != nullptr && !p.sb_scalar) sb = p.sb[n];
+      if (p.bias != nullptr) {
+        b = load_as_float(p.bias, p.bias_dtype, n);
+        if (p.epilogue == kEpiKitchen) {
+          if (p.out_dtype == kF16) b = round_through<kF16>(b);
+          if (p.out_dtype == kBF16) b = round_through<kBF16>(b);
+        }
+      }
+    }
+    wsb[c * 32 + lane] = sb;
+    wbias[c * 32 + lane] = b;
+  }
+  __syncwarp();
+  const float sa = (p.sa != nullptr && row < p.M) ? p.sa[row] : 0.0f;
+  uint32_t r0[32], r1[32];
+  __syncwarp();
+  tmem_ld32(taddr, r0);
+  tmem_ld_wait(r0);
+#pragma unroll 1
+  for (int c = 0; c < NC; c += 2) {
+    __syncwarp();
+    tmem_ld32(taddr + static_cast<uint32_t>((c + 1) * 32), r1);
+    store_dispatch<KIND>(p, r0, row, n0 + c * 32, sa, wsb + c * 32, wbias + c * 32);
+    __syncwarp();
+    tmem_ld_wait(r1);
+    if (c + 2 < NC) {
+      tmem_ld32(taddr + static_cast<uint32_t>((c + 2) * 32), r0);
+    } else {
+      release();  // all TMEM reads of this tile are complete
+    }
+    store_dispatch<KIND>(p, r1, row, n0 + (c + 1) * 32, sa, wsb + (c + 1) * 32,
+                         wbias + (c + 1) * 32);
+    __syncwarp();
+    if (c + 2 < NC) tmem_ld_wait(r0);
+  }
+}
+
+// --------------------------------------------------------- 1-CTA kernel
 template <int KIND, int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  const GemmParams p) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = Smem<128, BN, BN, STAGES>;
   constexpr int kKbElems = (KIND == kKindBF16) ? 64 : 128;  // 128 bytes of K per k-block
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -180,7 +256,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -221,6 +297,15 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
+      // Tail: wait until the MMA warp has released every slot, so no commit
+      // is still in flight to this CTA's barriers when it exits.
+      for (int i = 0; i < STAGES && ok; ++i) {
+        ok = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -259,46 +344,23 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int quarter = warp & 3;  // TMEM lanes this warp may access
+    float* wsb = reinterpret_cast<float*>(smem + L::kOffEpi) + (warp - 2) * 2 * BN;
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int buf = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
       const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
-      const int row = tm * 128 + quarter * 32 + lane;
-      const float sa = (p.sa != nullptr && row < p.M) ? p.sa[row] : 0.0f;
       bool ok = mbar_wait(&tfull[buf], use & 1u, abort_flag, kSiteEpilogue);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
-      const float sb_scalar = (p.sb != nullptr && p.sb_scalar) ? p.sb[0] : 0.0f;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n = tn * BN + c * 32;
-        // Lane j carries column n+j's scale and bias; store_chunk broadcasts.
-        float sb_lane = sb_scalar, bias_lane = 0.0f;
-        if (n + lane < p.N) {
-          if (p.sb != nullptr && !p.sb_scalar) sb_lane = p.sb[n + lane];
-          if (p.bias != nullptr) {
-            bias_lane = load_as_float(p.bias, p.bias_dtype, n + lane);
-            if (p.epilogue == kEpiKitchen) {
-              if (p.out_dtype == kF16) bias_lane = round_through<kF16>(bias_lane);
-              if (p.out_dtype == kBF16) bias_lane = round_through<kBF16>(bias_lane);
-            }
-          }
-        }
-        uint32_t r[32];
-        tmem_ld32(taddr + static_cast<uint32_t>(c * 32), r);
-        tmem_ld_wait(r);
-        if (c == BN / 32 - 1) {
-          // Accumulator fully read: hand the TMEM buffer back to the MMA warp.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[buf]);
-        }
-        store_dispatch<KIND>(p, r, row, n, sa, sb_lane, bias_lane);
-      }
+      epilogue_tile<KIND, BN>(p, taddr, tm * 128 + quarter * 32 + lane, tn * BN, lane, wsb, [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[buf]);
+      });
     }
   }
 
@@ -307,6 +369,168 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------- 2-CTA kernel
+// Cluster of two CTAs computes a 256 x BN tile: CTA r holds A rows
+// [128r, 128r+128) and B rows [r*BN/2, (r+1)*BN/2) of every k-block and
+// accumulates its 128 x BN half in its own TMEM.  The leader (rank 0) waits
+// on its `full` barrier (both CTAs' loads count there), issues the pair MMAs
+// and commits to both CTAs' `empty` / `tfull` barriers; both epilogues hand
+// TMEM back through the leader's `tempty` barrier (8 arrivals).
+template <int KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    qgemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
+                      const __grid_constant__ CUtensorMap tma_b, const GemmParams p) {
+  using L = Smem<128, BN / 2, BN, STAGES>;
+  constexpr int kKbElems = (KIND == kKindBF16) ? 64 : 128;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(cluster_id_x());
+  const int npairs = static_cast<int>(cluster_count_x());
+  const int num_tiles = p.tiles_m * p.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_a);
+    tma_prefetch_desc(&tma_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, L::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t full_leader = mapa_shared(smem_u32(&full[0]), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+          const uint32_t fb = full_leader + static_cast<uint32_t>(stage * 8);
+          tma_load_2d_pair(&tma_a, fb, smem + L::kOffA + stage * L::kABytes, kb * kKbElems,
+                           tm * 256 + static_cast<int>(rank) * 128);
+          tma_load_2d_pair(&tma_b, fb, smem + L::kOffB + stage * L::kBBytes, kb * kKbElems,
+                           tn * BN + static_cast<int>(rank) * (BN / 2));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Tail: every slot released by the leader's commits before exit.
+      for (int i = 0; i < STAGES && ok; ++i) {
+        ok = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = make_idesc<KIND>(256, BN);
+      const uint32_t peer_empty = mapa_shared(smem_u32(&empty[0]), 1);
+      const uint32_t peer_tfull = mapa_shared(smem_u32(&tfull[0]), 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int t = 0;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++t) {
+        const int buf = t & 1;
+        const uint32_t use = static_cast<uint32_t>(t >> 1);
+        if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag, kSiteMmaTmem)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L::kOffA + stage * L::kABytes);
+          const uint32_t b_addr = smem_u32(smem + L::kOffB + stage * L::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_pair<KIND>(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32),
+                            idesc, (kb | kk) != 0 ? 1u : 0u);
+          umma_commit_pair(smem_u32(&empty[stage]));
+          umma_commit_pair(peer_empty + static_cast<uint32_t>(stage * 8));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&tfull[buf]));
+        umma_commit_pair(peer_tfull + static_cast<uint32_t>(buf * 8));
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    float* wsb = reinterpret_cast<float*>(smem + L::kOffEpi) + (warp - 2) * 2 * BN;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+    int t = 0;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++t) {
+      const int buf = t & 1;
+      const uint32_t use = static_cast<uint32_t>(t >> 1);
+      const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+      bool ok = mbar_wait(&tfull[buf], use & 1u, abort_flag, kSiteEpilogue);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      const int row = tm * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
+      epilogue_tile<KIND, BN>(p, taddr, row, tn * BN, lane, wsb, [&] {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader + static_cast<uint32_t>(buf * 8));
+      });
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still touch its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, L::kTmemCols);
   }
 }
 
@@ -349,9 +573,14 @@ static cudaError_t make_kmajor_map(CUtensorMap* map, const void* ptr, int elem_b
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-int device_sm_count() {
+static int current_device() {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+int device_sm_count() {
+  const int dev = current_device();
   static int cache[64] = {0};
   if (dev < 64 && cache[dev] > 0) return cache[dev];
   int n = 0;
@@ -361,62 +590,142 @@ int device_sm_count() {
   return n;
 }
 
+template <typename Kernel>
+static cudaError_t configure_once(Kernel kernel, int smem_bytes, bool* done) {
+  const int dev = current_device();
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  if (!done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+    if (e != cudaSuccess) return e;
+    done[dev] = true;
+  }
+  return cudaSuccess;
+}
+
 template <int KIND, int BN, int STAGES>
-static cudaError_t launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, GemmParams p,
-                               int max_ctas, cudaStream_t stream) {
-  using L = GemmSmem<BN, STAGES>;
+static cudaError_t launch_single(const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams p,
+                                 int max_ctas, cudaStream_t stream) {
+  using L = Smem<128, BN, BN, STAGES>;
   auto kernel = qgemm_kernel<KIND, BN, STAGES>;
   static bool configured[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 64) return cudaErrorInvalidDevice;
-  if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
-    if (e != cudaSuccess) return e;
-    configured[dev] = true;
-  }
+  cudaError_t e = configure_once(kernel, L::kAlloc, configured);
+  if (e != cudaSuccess) return e;
+  const int eb = KIND == kKindBF16 ? 2 : 1;
+  CUtensorMap ma, mb;
+  if ((e = make_kmajor_map(&ma, a, eb, p.K, p.M, lda * eb, 128)) != cudaSuccess) return e;
+  if ((e = make_kmajor_map(&mb, b, eb, p.K, p.N, ldb * eb, BN)) != cudaSuccess) return e;
+  p.tiles_m = static_cast<int>((p.M + 127) / 128);
   p.tiles_n = static_cast<int>((p.N + BN - 1) / BN);
   const int tiles = p.tiles_m * p.tiles_n;
   int grid = device_sm_count();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
-  if (grid <= 0) return cudaSuccess;
   kernel<<<grid, 192, L::kAlloc, stream>>>(ma, mb, p);
   return cudaGetLastError();
 }
 
-// Pick the N tile so a persistent wave stays full: wide tiles (more operand
-// reuse per MMA) unless they leave most SMs idle.
-static int choose_bn(int64_t M, int64_t N) {
-  const int64_t tm = (M + 127) / 128;
-  const int sms = device_sm_count();
-  if (N <= 128) return 128;
-  if (tm * ((N + 255) / 256) >= sms) return 256;
-  return tm * ((N + 127) / 128) > tm * ((N + 255) / 256) ? 128 : 256;
+template <int KIND, int BN, int STAGES>
+static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams p,
+                               int max_ctas, cudaStream_t stream) {
+  using L = Smem<128, BN / 2, BN, STAGES>;
+  auto kernel = qgemm_pair_kernel<KIND, BN, STAGES>;
+  static bool configured[64] = {false};
+  static int max_pairs[64] = {0};
+  cudaError_t e = configure_once(kernel, L::kAlloc, configured);
+  if (e != cudaSuccess) return e;
+  const int dev = current_device();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_pairs[dev] == 0) {
+    cfg.gridDim = dim3(2 * (device_sm_count() / 2));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = -1;
+    }
+    max_pairs[dev] = n;
+  }
+  if (max_pairs[dev] < 0) return cudaErrorNotSupported;
+  const int eb = KIND == kKindBF16 ? 2 : 1;
+  CUtensorMap ma, mb;
+  if ((e = make_kmajor_map(&ma, a, eb, p.K, p.M, lda * eb, 128)) != cudaSuccess) return e;
+  if ((e = make_kmajor_map(&mb, b, eb, p.K, p.N, ldb * eb, BN / 2)) != cudaSuccess) return e;
+  p.tiles_m = static_cast<int>((p.M + 255) / 256);
+  p.tiles_n = static_cast<int>((p.N + BN - 1) / BN);
+  const int tiles = p.tiles_m * p.tiles_n;
+  int pairs = max_pairs[dev];
+  if (max_ctas > 0 && max_ctas / 2 < pairs) pairs = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
+  if (tiles < pairs) pairs = tiles;
+  cfg.gridDim = dim3(2 * pairs);
+  e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
+
+// Wave-quantization aware N tile for the pair kernel: among 256 and 192
+// choose the one whose persistent waves are fullest.
+static int choose_pair_bn(int64_t M, int64_t N, int pairs) {
+  const int64_t tm = (M + 255) / 256;
+  double best = -1.0;
+  int bn = 256;
+  for (int cand : {256, 192}) {
+    const int64_t tiles = tm * ((N + cand - 1) / cand);
+    const int64_t waves = (tiles + pairs - 1) / pairs;
+    const double eff = static_cast<double>(tiles) / static_cast<double>(waves * pairs) *
+                       (cand == 256 ? 1.0 : 0.97);
+    if (eff > best + 1e-9) {
+      best = eff;
+      bn = cand;
+    }
+  }
+  return bn;
+}
+
+static int g_force_path = 0;  // 0 auto, 1 single-CTA only, 2 pair only
 
 cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams p,
                       int max_ctas, cudaStream_t stream) {
   if (p.M == 0 || p.N == 0) return cudaSuccess;
   const int eb = kind == kKindBF16 ? 2 : 1;
-  const int bn = choose_bn(p.M, p.N);
-  CUtensorMap ma, mb;
-  cudaError_t e = make_kmajor_map(&ma, a, eb, p.K, p.M, lda * eb, 128);
-  if (e != cudaSuccess) return e;
-  e = make_kmajor_map(&mb, b, eb, p.K, p.N, ldb * eb, bn);
-  if (e != cudaSuccess) return e;
-  p.tiles_m = static_cast<int>((p.M + 127) / 128);
   const int kb_elems = 128 / eb;
   p.num_kb = static_cast<int>((p.K + kb_elems - 1) / kb_elems);
+  const bool pair = g_force_path == 2 || (g_force_path == 0 && p.M > 128);
+  if (pair) {
+    const int bn = choose_pair_bn(p.M, p.N, device_sm_count() / 2);
+    cudaError_t e;
+    if (kind == kKindI8)
+      e = bn == 256 ? launch_pair<kKindI8, 256, 6>(a, lda, b, ldb, p, max_ctas, stream)
+                    : launch_pair<kKindI8, 192, 7>(a, lda, b, ldb, p, max_ctas, stream);
+    else if (kind == kKindE4M3)
+      e = bn == 256 ? launch_pair<kKindE4M3, 256, 6>(a, lda, b, ldb, p, max_ctas, stream)
+                    : launch_pair<kKindE4M3, 192, 7>(a, lda, b, ldb, p, max_ctas, stream);
+    else
+      e = bn == 256 ? launch_pair<kKindBF16, 256, 6>(a, lda, b, ldb, p, max_ctas, stream)
+                    : launch_pair<kKindBF16, 192, 7>(a, lda, b, ldb, p, max_ctas, stream);
+    if (e != cudaErrorNotSupported || g_force_path == 2) return e;
+  }
+  // Single-CTA tiles: 256 wide when that still fills the machine, else 128.
+  const int64_t tm = (p.M + 127) / 128;
+  const bool wide = p.N > 128 && tm * ((p.N + 255) / 256) >= device_sm_count();
   if (kind == kKindI8)
-    return bn == 256 ? launch_gemm<kKindI8, 256, 4>(ma, mb, p, max_ctas, stream)
-                     : launch_gemm<kKindI8, 128, 6>(ma, mb, p, max_ctas, stream);
+    return wide ? launch_single<kKindI8, 256, 4>(a, lda, b, ldb, p, max_ctas, stream)
+                : launch_single<kKindI8, 128, 6>(a, lda, b, ldb, p, max_ctas, stream);
   if (kind == kKindE4M3)
-    return bn == 256 ? launch_gemm<kKindE4M3, 256, 4>(ma, mb, p, max_ctas, stream)
-                     : launch_gemm<kKindE4M3, 128, 6>(ma, mb, p, max_ctas, stream);
-  return bn == 256 ? launch_gemm<kKindBF16, 256, 4>(ma, mb, p, max_ctas, stream)
-                   : launch_gemm<kKindBF16, 128, 6>(ma, mb, p, max_ctas, stream);
+    return wide ? launch_single<kKindE4M3, 256, 4>(a, lda, b, ldb, p, max_ctas, stream)
+                : launch_single<kKindE4M3, 128, 6>(a, lda, b, ldb, p, max_ctas, stream);
+  return wide ? launch_single<kKindBF16, 256, 4>(a, lda, b, ldb, p, max_ctas, stream)
+              : launch_single<kKindBF16, 128, 6>(a, lda, b, ldb, p, max_ctas, stream);
 }
+
+void set_gemm_path(int path) { g_force_path = path; }
 
 }  // namespace b2
 

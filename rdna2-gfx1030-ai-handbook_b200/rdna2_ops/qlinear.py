@@ -30,6 +30,14 @@ EPILOGUES = {"separate": nat.EPI_SEPARATE, "fused": nat.EPI_FMA, "kitchen": nat.
 FLOAT_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 
 
+def set_gemm_path(path):
+    """Process-wide GEMM kernel choice: "auto", "single" (1-CTA 128-row
+    tiles) or "pair" (2-CTA cta_group::2 256-row tiles).  Results are
+    bit-identical; this is a tuning and verification knob."""
+    code = {"auto": 0, "single": 1, "pair": 2}[path]
+    nat.check(nat.library().b2_set_gemm_path(code), "b2_set_gemm_path")
+
+
 def _round_up(v, m):
     return (v + m - 1) // m * m
 

@@ -47,6 +47,13 @@ def x_bits(xt):
     return bits(xt)
 
 
+@pytest.fixture(params=["single", "pair"])
+def gemm_path(request):
+    qlinear.set_gemm_path(request.param)
+    yield request.param
+    qlinear.set_gemm_path("auto")
+
+
 @pytest.fixture(autouse=True, scope="module")
 def _device_status_clean():
     nat.device_status(reset=True)
@@ -57,7 +64,7 @@ def _device_status_clean():
 # ------------------------------------------------------- golden: INT8 GEMM
 @pytest.mark.parametrize("key", ["weight_nk_vector", "weight_nk_scalar", "rhs_kn_vector",
                                  "rhs_kn_scalar"])
-def test_int8_known_answer(golden, key):
+def test_int8_known_answer(golden, key, gemm_path):
     """bench_int8_gemm.py:181-203 on the GPU: offset+padded A view, weight.T view
     and contiguous [K,N] B, INT32 exact, FP32 dequant bitwise."""
     g = golden("int8_known_answer.npz")
@@ -72,9 +79,9 @@ def test_int8_known_answer(golden, key):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 1, 1), (1, 16, 16), (37, 53, 79), (129, 257, 33),
-                                   (128, 256, 128), (300, 200, 1000), (513, 640, 3072),
+                                   (128, 256, 128), (300, 200, 1000), (513, 640, 3072), (1024, 9472, 384),
                                    (64, 96, 131071 // 8)])
-def test_int8_matmul_exact(m, n, k):
+def test_int8_matmul_exact(m, n, k, gemm_path):
     rng = np.random.default_rng(m * 7 + n * 3 + k)
     a = rng.integers(-128, 128, (m, k), dtype=np.int8)
     w = rng.integers(-128, 128, (n, k), dtype=np.int8)
@@ -85,7 +92,7 @@ def test_int8_matmul_exact(m, n, k):
     assert np.array_equal(got2.cpu().numpy(), ref)
 
 
-def test_int8_accumulator_extremes():
+def test_int8_accumulator_extremes(gemm_path):
     k = 4096
     a = np.full((130, k), -128, np.int8)
     w = np.full((140, k), -128, np.int8)
@@ -97,7 +104,7 @@ def test_int8_accumulator_extremes():
 @pytest.mark.parametrize("rounding", ["separate", "fused"])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("scalar", [False, True])
-def test_int8_gemm_dequant_epilogues(rounding, out_dtype, scalar):
+def test_int8_gemm_dequant_epilogues(rounding, out_dtype, scalar, gemm_path):
     rng = np.random.default_rng(11)
     m, n, k = 200, 264, 512
     a = rng.integers(-127, 128, (m, k), dtype=np.int8)
@@ -161,7 +168,7 @@ def _weights(rng, n, k, block):
                                          (333, 4000, 1024, 128)])
 @pytest.mark.parametrize("epilogue", ["separate", "kitchen", "fused"])
 @pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16, torch.float32])
-def test_w8a8_linear_bit_exact(m, n, k, block, epilogue, out_dtype):
+def test_w8a8_linear_bit_exact(m, n, k, block, epilogue, out_dtype, gemm_path):
     rng = np.random.default_rng(m + n + k)
     x32 = outlier_activations(rng, m, k)
     _, wq, sw = _weights(rng, n, k, block)
@@ -224,7 +231,7 @@ def test_config2_full_size_sampled_and_deterministic():
 
 # -------------------------------------------------------------------- FP8
 @pytest.mark.parametrize("m", [1, 2048])
-def test_fp8_linear_matches_fp64_oracle(m):
+def test_fp8_linear_matches_fp64_oracle(m, gemm_path):
     """BASELINE config 4 (A bf16 -> e4m3 per token, W e4m3 per channel, bf16
     out; K = N = 5120, plus the M = 1 decode shape).  Codes bit-exact; outputs
     within 1 bf16 ulp plus 2^-12 of the summed |products| (fp32 accumulation
