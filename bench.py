@@ -45,8 +45,8 @@ SEED = 20261106
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=500)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -142,13 +142,15 @@ def run_reference(args, rank):
 
 # ----------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples SM clock and throttle reasons with NVML while the timed region runs."""
+    """Samples SM clock, power and clock-event reasons with NVML every 5 ms
+    while the timed region runs (same fields as the nvidia-smi clocks query)."""
 
     NAMES = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
              "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, index):
-        self.samples, self.reasons, self.stop_evt = [], set(), threading.Event()
+        self.samples, self.power, self.reasons = [], [], set()
+        self.stop_evt = threading.Event()
         self.max_mhz = None
         try:
             import pynvml
@@ -163,13 +165,14 @@ class ClockSampler:
         while not self.stop_evt.is_set():
             try:
                 self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+                self.power.append(self.nvml.nvmlDeviceGetPowerUsage(self.h) / 1000.0)
                 mask = self.nvml.nvmlDeviceGetCurrentClocksEventReasons(self.h)
                 for name, bit in self.NAMES.items():
                     if mask & bit:
                         self.reasons.add(name)
             except Exception:
                 break
-            time.sleep(0.02)
+            time.sleep(0.005)
 
     def __enter__(self):
         if self.nvml:
@@ -184,7 +187,9 @@ class ClockSampler:
 
     def summary(self):
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_mhz_min": min(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "power_w_max": max(self.power) if self.power else None,
                 "samples": len(self.samples)}
 
 

@@ -42,9 +42,16 @@ const char* b2_error_string(int status);
  * device. */
 int b2_sm_count(void);
 
-/* Process-wide GEMM kernel selection: 0 = automatic (2-CTA pair kernel when
- * M > 128, else single-CTA), 1 = single-CTA kernel only, 2 = pair kernel
- * only.  A tuning and verification knob; results are identical either way.
+/* Number of 2-CTA clusters of the pair GEMM kernel that fit on the current
+ * device at once (its persistent grid, in pairs), or -1 when cluster launch
+ * is unavailable. */
+int b2_pair_capacity(void);
+
+/* Process-wide GEMM kernel selection: 0 = automatic (pair or single tiles by
+ * a persistent-wave time model), 1 = single-CTA kernel, 2 = pair kernel (both
+ * with automatic N tile), 3 = single N=256, 4 = single N=128, 5 = pair
+ * N=256, 6 = pair N=192.  A tuning and verification knob; results are
+ * identical for every choice.
  * No reference counterpart (the reference exposes tile keywords instead,
  * rdna2_ops/int8_gemm.py:195-214). */
 int b2_set_gemm_path(int path);

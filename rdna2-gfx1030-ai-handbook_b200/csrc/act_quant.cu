@@ -19,189 +19,283 @@
 
 namespace b2 {
 
+// Raw 16-byte (two for fp32) chunk of 8 consecutive elements of one lane.
+struct Raw8 {
+  uint4 a, b;
+};
+
 template <int DT>
-__device__ __forceinline__ void load8(const void* x, int64_t off, bool vec, int valid, float (&v)[8]) {
+__device__ __forceinline__ void load_raw(const void* x, int64_t off, bool vec, int valid, Raw8& r) {
   if (vec && valid == 8) {
     if constexpr (DT == kF32) {
-      const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(x) + off);
-      const float4 a = __ldg(p), b = __ldg(p + 1);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(x) + off);
+      r.a = __ldg(p);
+      r.b = __ldg(p + 1);
     } else {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off));
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if constexpr (DT == kF16) {
-          const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-          v[2 * i] = __low2float(h);
-          v[2 * i + 1] = __high2float(h);
-        } else {
-          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
-          v[2 * i] = __low2float(h);
-          v[2 * i + 1] = __high2float(h);
-        }
-      }
+      r.a = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off));
     }
   } else {
+    // Ragged tail, unaligned rows or dead rows: element loads, zero padding.
+    uint32_t w[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = j < valid ? load_as_float(x, DT, off + j) : 0.0f;
+    for (int j = 0; j < 8; ++j) {
+      float f = j < valid ? load_as_float(x, DT, off + j) : 0.0f;
+      if constexpr (DT == kF32) {
+        w[j] = __float_as_uint(f);
+      } else if constexpr (DT == kF16) {
+        w[j] = __half_as_ushort(__float2half_rn(f));  // exact: f came from fp16
+      } else {
+        w[j] = __bfloat16_as_ushort(__float2bfloat16_rn(f));
+      }
+    }
+    if constexpr (DT == kF32) {
+      r.a = make_uint4(w[0], w[1], w[2], w[3]);
+      r.b = make_uint4(w[4], w[5], w[6], w[7]);
+    } else {
+      r.a = make_uint4(w[0] | (w[1] << 16), w[2] | (w[3] << 16), w[4] | (w[5] << 16),
+                       w[6] | (w[7] << 16));
+    }
   }
+}
+
+template <int DT>
+__device__ __forceinline__ void unpack_raw(const Raw8& r, float (&v)[8]) {
+  if constexpr (DT == kF32) {
+    v[0] = __uint_as_float(r.a.x); v[1] = __uint_as_float(r.a.y);
+    v[2] = __uint_as_float(r.a.z); v[3] = __uint_as_float(r.a.w);
+    v[4] = __uint_as_float(r.b.x); v[5] = __uint_as_float(r.b.y);
+    v[6] = __uint_as_float(r.b.z); v[7] = __uint_as_float(r.b.w);
+  } else {
+    const uint32_t w[4] = {r.a.x, r.a.y, r.a.z, r.a.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if constexpr (DT == kF16) {
+        const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+        v[2 * i] = __low2float(h);
+        v[2 * i + 1] = __high2float(h);
+      } else {
+        const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+        v[2 * i] = __low2float(h);
+        v[2 * i + 1] = __high2float(h);
+      }
+    }
+  }
+}
+
+// Exact quantizers: clamp(rint(RN(v/s))) for int8, e4m3_rn_sat(RN(v/s)).
+// Fast path multiplies by r = RN(1/s): y = RN(v*r) lies within 2^-22
+// relative of the exact quotient, as does RN(v/s), and rounding to the
+// target grid is monotone, so whenever y is farther than a safety margin
+// from a rounding boundary both give the same code.  Near a boundary (a few
+// elements in 10^4) the correctly rounded IEEE quotient decides.
+__device__ __forceinline__ uint32_t slow_int8(float v, float s) {
+  int q = __float2int_rn(__fdiv_rn(v, s));
+  q = q > 127 ? 127 : (q < -127 ? -127 : q);
+  return static_cast<uint32_t>(q) & 0xffu;
+}
+
+// Returns a word whose low byte is the int8 code.
+__device__ __forceinline__ uint32_t quant_int8(float v, float s, float r, bool fast) {
+  const float y = __fmul_rn(v, r);               // |y| <= 127 * (1 + 2^-22)
+  const float m = __fadd_rn(y, 12582912.0f);     // 1.5 * 2^23: rounds y to an integer (ties even)
+  const float n = __fsub_rn(m, 12582912.0f);     // rint(y), exact
+  if (fast && fabsf(__fsub_rn(n, y)) < 0.4998779296875f) {  // 0.5 - 2^-13 margin
+    return __float_as_uint(m);                   // low byte = n mod 256, |n| <= 127
+  }
+  return slow_int8(v, s);
+}
+
+__device__ __forceinline__ uint32_t quant_e4m3(float v, float s, float r, bool fast) {
+  if (fast) {
+    const float y = __fmul_rn(v, r);
+    const float d = __fmul_rn(fabsf(y), 9.5367431640625e-07f);  // 2^-20 relative margin
+    const uint32_t lo = __nv_cvt_float_to_fp8(__fsub_rn(y, d), __NV_SATFINITE, __NV_E4M3);
+    const uint32_t hi = __nv_cvt_float_to_fp8(__fadd_rn(y, d), __NV_SATFINITE, __NV_E4M3);
+    if (lo == hi) return lo;
+  }
+  return static_cast<uint32_t>(__nv_cvt_float_to_fp8(__fdiv_rn(v, s), __NV_SATFINITE, __NV_E4M3));
 }
 
 template <int QUANT>
-__device__ __forceinline__ uint32_t encode(float v, float s) {
-  const float z = __fdiv_rn(v, s);
-  if constexpr (QUANT == 0) {
-    int q = __float2int_rn(z);
-    q = q > 127 ? 127 : (q < -127 ? -127 : q);
-    return static_cast<uint32_t>(q) & 0xffu;
-  } else {
-    return static_cast<uint32_t>(__nv_cvt_float_to_fp8(z, __NV_SATFINITE, __NV_E4M3));
-  }
+__device__ __forceinline__ uint32_t pack4(const float* v, float s, float r, bool fast) {
+  uint32_t c[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    c[i] = QUANT == 0 ? quant_int8(v[i], s, r, fast) : quant_e4m3(v[i], s, r, fast);
+  return __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
 }
 
+// Persistent grid-stride kernel: a CTA of 4 warps handles 4/wpr rows per
+// iteration (wpr warps per row, SPW 256-element segments per warp), and
+// prefetches the next iteration's segments into registers before rotating
+// and quantizing the current ones.
 template <int DT, int SPW, int QUANT>
 __global__ void __launch_bounds__(128)
     act_quant_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int wpr, int block,
                      float inv, uint8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale,
                      int vec_in, int vec_out) {
-  __shared__ float s_max[4];
+  __shared__ float s_max[2][4];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * (4 / wpr) + warp / wpr;
-  const int part = warp % wpr;
-  const bool live = row < M;
+  const int groups = 4 / wpr;
+  const int g = warp / wpr, part = warp % wpr;
   const int64_t seg0 = static_cast<int64_t>(part) * SPW;
+  const int64_t row_step = static_cast<int64_t>(gridDim.x) * groups;
 
-  float v[SPW][8];
+  auto issue = [&](int64_t row, Raw8 (&raw)[SPW]) {
+    const bool live = row < M;
 #pragma unroll
-  for (int s = 0; s < SPW; ++s) {
-    const int64_t k0 = (seg0 + s) * 256 + lane * 8;
-    int64_t rem = static_cast<int64_t>(K) - k0;
-    const int valid = live ? static_cast<int>(rem < 0 ? 0 : (rem > 8 ? 8 : rem)) : 0;
-    load8<DT>(x, live ? static_cast<int64_t>(row) * ldx + k0 : 0, vec_in != 0, valid, v[s]);
-  }
+    for (int s = 0; s < SPW; ++s) {
+      const int64_t k0 = (seg0 + s) * 256 + lane * 8;
+      const int64_t rem = static_cast<int64_t>(K) - k0;
+      const int valid = live ? static_cast<int>(rem < 0 ? 0 : (rem > 8 ? 8 : rem)) : 0;
+      load_raw<DT>(x, live ? row * ldx + k0 : 0, vec_in != 0, valid, raw[s]);
+    }
+  };
 
-  if (block > 1) {
+  Raw8 raw[SPW];
+  int64_t base = static_cast<int64_t>(blockIdx.x) * groups;
+  issue(base + g, raw);
+  int parity = 0;
+  for (; base < M; base += row_step) {
+    const int64_t row = base + g;
+    const bool live = row < M;
+    float v[SPW][8];
 #pragma unroll
-    for (int h = 1; h < 8; h <<= 1) {
-      if (block > h) {
+    for (int s = 0; s < SPW; ++s) unpack_raw<DT>(raw[s], v[s]);
+    if (base + row_step < M) issue(base + row_step + g, raw);  // next rows in flight
+
+    if (block > 1) {
 #pragma unroll
-        for (int s = 0; s < SPW; ++s)
+      for (int h = 1; h < 8; h <<= 1) {
+        if (block > h) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            if (!(i & h)) {
-              const float a = v[s][i], b = v[s][i + h];
-              v[s][i] = __fadd_rn(a, b);
-              v[s][i + h] = __fsub_rn(a, b);
-            }
+          for (int s = 0; s < SPW; ++s)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              if (!(i & h)) {
+                const float a = v[s][i], b = v[s][i + h];
+                v[s][i] = __fadd_rn(a, b);
+                v[s][i + h] = __fsub_rn(a, b);
+              }
+        }
       }
-    }
 #pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      if (block > 8 * d) {
-        const bool upper = (lane & d) != 0;
+      for (int d = 1; d < 32; d <<= 1) {
+        if (block > 8 * d) {
+          // lower lane: v + o; upper lane: o - v.  fma(+-1, v, o) rounds once,
+          // exactly like the add/sub it replaces.
+          const float sgn = (lane & d) ? -1.0f : 1.0f;
 #pragma unroll
-        for (int s = 0; s < SPW; ++s)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float o = __shfl_xor_sync(0xffffffffu, v[s][i], d);
-            v[s][i] = upper ? __fsub_rn(o, v[s][i]) : __fadd_rn(v[s][i], o);
-          }
-      }
-    }
-#pragma unroll
-    for (int ds = 1; ds < SPW; ds <<= 1) {
-      if (block > 256 * ds) {
-#pragma unroll
-        for (int s = 0; s < SPW; ++s)
-          if (!(s & ds) && s + ds < SPW) {
+          for (int s = 0; s < SPW; ++s)
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const float a = v[s][i], b = v[s + ds][i];
-              v[s][i] = __fadd_rn(a, b);
-              v[s + ds][i] = __fsub_rn(a, b);
+              const float o = __shfl_xor_sync(0xffffffffu, v[s][i], d);
+              v[s][i] = __fmaf_rn(sgn, v[s][i], o);
             }
-          }
+        }
       }
+#pragma unroll
+      for (int ds = 1; ds < SPW; ds <<= 1) {
+        if (block > 256 * ds) {
+#pragma unroll
+          for (int s = 0; s < SPW; ++s)
+            if (!(s & ds) && s + ds < SPW) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float a = v[s][i], b = v[s + ds][i];
+                v[s][i] = __fadd_rn(a, b);
+                v[s + ds][i] = __fsub_rn(a, b);
+              }
+            }
+        }
+      }
+#pragma unroll
+      for (int s = 0; s < SPW; ++s)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[s][i] = __fmul_rn(v[s][i], inv);
     }
+
+    float amax = 0.0f;
 #pragma unroll
     for (int s = 0; s < SPW; ++s)
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[s][i] = __fmul_rn(v[s][i], inv);
-  }
-
-  float amax = 0.0f;
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[s][i]));
 #pragma unroll
-  for (int s = 0; s < SPW; ++s)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[s][i]));
-#pragma unroll
-  for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
-  if (wpr > 1) {
-    if (lane == 0) s_max[warp] = amax;
-    __syncthreads();
-    const int first = (warp / wpr) * wpr;
-    for (int w = 0; w < wpr; ++w) amax = fmaxf(amax, s_max[first + w]);
-  }
-  float sc = __fdiv_rn(amax, QUANT == 0 ? 127.0f : 448.0f);
-  if (!(sc > 0.0f)) sc = 1.0f;
-  if (!live) return;
-
-#pragma unroll
-  for (int s = 0; s < SPW; ++s) {
-    const int64_t k0 = (seg0 + s) * 256 + lane * 8;
-    if (k0 >= K) continue;
-    uint8_t* dst = q + static_cast<int64_t>(row) * ldq + k0;
-    if (vec_out && k0 + 8 <= K) {
-      uint32_t lo = 0, hi = 0;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        lo |= encode<QUANT>(v[s][i], sc) << (8 * i);
-        hi |= encode<QUANT>(v[s][i + 4], sc) << (8 * i);
-      }
-      *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (k0 + i < K) dst[i] = static_cast<uint8_t>(encode<QUANT>(v[s][i], sc));
+    for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+    if (wpr > 1) {
+      if (lane == 0) s_max[parity][warp] = amax;
+      __syncthreads();
+      for (int w = 0; w < wpr; ++w) amax = fmaxf(amax, s_max[parity][g * wpr + w]);
+      parity ^= 1;
     }
+    float sc = __fdiv_rn(amax, QUANT == 0 ? 127.0f : 448.0f);
+    if (!(sc > 0.0f)) sc = 1.0f;
+    if (!live) continue;
+    const float rcp = __frcp_rn(sc);
+    const bool fast = sc > 1e-30f && sc < 1e30f;
+
+#pragma unroll
+    for (int s = 0; s < SPW; ++s) {
+      const int64_t k0 = (seg0 + s) * 256 + lane * 8;
+      if (k0 >= K) continue;
+      uint8_t* dst = q + row * ldq + k0;
+      const uint32_t lo = pack4<QUANT>(&v[s][0], sc, rcp, fast);
+      const uint32_t hi = pack4<QUANT>(&v[s][4], sc, rcp, fast);
+      if (vec_out && k0 + 8 <= K) {
+        *reinterpret_cast<uint2*>(dst) = make_uint2(lo, hi);
+      } else {
+        for (int i = 0; i < 8 && k0 + i < K; ++i)
+          dst[i] = static_cast<uint8_t>((i < 4 ? lo >> (8 * i) : hi >> (8 * (i - 4))) & 0xffu);
+      }
+    }
+    if (part == 0 && lane == 0) scale[row] = sc;
   }
-  if (part == 0 && lane == 0) scale[row] = sc;
+}
+
+template <int DT, int SPW, int QUANT>
+static cudaError_t launch_one(int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K, int wpr,
+                              int block, float inv, uint8_t* q, int64_t ldq, float* scale, int vin,
+                              int vout) {
+  auto kernel = act_quant_kernel<DT, SPW, QUANT>;
+  static int per_sm[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && per_sm[dev] == 0) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, 128, 0) != cudaSuccess || n <= 0) n = 4;
+    per_sm[dev] = n;
+  }
+  const int groups = 4 / wpr;
+  const int64_t need = (M + groups - 1) / groups;
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * (dev < 64 ? per_sm[dev] : 4);
+  const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
+  kernel<<<grid, 128, 0, st>>>(x, ldx, static_cast<int>(M), K, wpr, block, inv, q, ldq, scale, vin,
+                               vout);
+  return cudaGetLastError();
 }
 
 template <int DT, int QUANT>
-static cudaError_t launch_spw(int spw, dim3 grid, cudaStream_t st, const void* x, int64_t ldx, int M,
-                             int K, int wpr, int block, float inv, uint8_t* q, int64_t ldq,
-                             float* scale, int vin, int vout) {
-#define B2_SPW_CASE(S)                                                                          \
-  case S:                                                                                       \
-    act_quant_kernel<DT, S, QUANT><<<grid, 128, 0, st>>>(x, ldx, M, K, wpr, block, inv, q, ldq, \
-                                                          scale, vin, vout);                    \
-    break;
+static cudaError_t launch_spw(int spw, int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K,
+                             int wpr, int block, float inv, uint8_t* q, int64_t ldq, float* scale,
+                             int vin, int vout) {
+#define B2_SPW_CASE(S) \
+  case S:              \
+    return launch_one<DT, S, QUANT>(M, st, x, ldx, K, wpr, block, inv, q, ldq, scale, vin, vout);
   switch (spw) {
     B2_SPW_CASE(1) B2_SPW_CASE(2) B2_SPW_CASE(3) B2_SPW_CASE(4) B2_SPW_CASE(5) B2_SPW_CASE(6)
     B2_SPW_CASE(7) B2_SPW_CASE(8) B2_SPW_CASE(10) B2_SPW_CASE(12) B2_SPW_CASE(16)
     default: return cudaErrorInvalidValue;
   }
 #undef B2_SPW_CASE
-  return cudaGetLastError();
 }
 
-// Pick warps-per-row and segments-per-warp: fewest warps whose registers hold
-// the row, with warp ranges aligned to the rotation block.
+// Pick warps-per-row and segments-per-warp: the fewest segments per lane
+// (registers, hence occupancy) that cover the row with up to 4 warps, warp
+// ranges aligned to the rotation block.
 static bool choose_layout(int64_t K, int block, int* wpr, int* spw) {
-  // Up to 12 segments (96 fp32 values) per lane stay in registers without
-  // spilling; 16 is the last resort for 12288 < K <= 16384.
-  static const int kSpw[] = {1, 2, 3, 4, 5, 6, 7, 8, 10, 12};
-  for (int w : {1, 2, 4, 5}) {
-    if (w == 5) {
-      if (K > 4 * 16 * 256 || (block > 1 && (block > 16 * 256 || (16 * 256) % block != 0))) return false;
-      *wpr = 4;
-      *spw = 16;
-      return true;
-    }
-    for (int s : kSpw) {
+  static const int kSpw[] = {1, 2, 3, 4, 5, 6, 7, 8, 10, 12, 16};
+  for (int s : kSpw) {
+    for (int w : {1, 2, 4}) {
       if (static_cast<int64_t>(w) * s * 256 < K) continue;
       if (block > 1 && block > s * 256) continue;
       if (block > 1 && w > 1 && (s * 256) % block != 0) continue;
@@ -222,18 +316,16 @@ cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   const int vin = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ldx * eb) % 16 == 0);
   const int vout = (reinterpret_cast<uintptr_t>(q) % 8 == 0) && (ldq % 8 == 0);
   const float inv = block > 1 ? static_cast<float>(1.0 / sqrt(static_cast<double>(block))) : 1.0f;
-  const int rows_per_cta = 4 / wpr;
-  const dim3 grid(static_cast<unsigned>((M + rows_per_cta - 1) / rows_per_cta));
   uint8_t* qb = static_cast<uint8_t*>(q);
-  const int m = static_cast<int>(M), k = static_cast<int>(K);
+  const int k = static_cast<int>(K);
   if (quant == 0) {
-    if (x_dtype == kF32) return launch_spw<kF32, 0>(spw, grid, stream, x, ldx, m, k, wpr, block, inv, qb, ldq, scale, vin, vout);
-    if (x_dtype == kF16) return launch_spw<kF16, 0>(spw, grid, stream, x, ldx, m, k, wpr, block, inv, qb, ldq, scale, vin, vout);
-    return launch_spw<kBF16, 0>(spw, grid, stream, x, ldx, m, k, wpr, block, inv, qb, ldq, scale, vin, vout);
+    if (x_dtype == kF32) return launch_spw<kF32, 0>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
+    if (x_dtype == kF16) return launch_spw<kF16, 0>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
+    return launch_spw<kBF16, 0>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
   }
-  if (x_dtype == kF32) return launch_spw<kF32, 1>(spw, grid, stream, x, ldx, m, k, wpr, block, inv, qb, ldq, scale, vin, vout);
-  if (x_dtype == kF16) return launch_spw<kF16, 1>(spw, grid, stream, x, ldx, m, k, wpr, block, inv, qb, ldq, scale, vin, vout);
-  return launch_spw<kBF16, 1>(spw, grid, stream, x, ldx, m, k, wpr, block, inv, qb, ldq, scale, vin, vout);
+  if (x_dtype == kF32) return launch_spw<kF32, 1>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
+  if (x_dtype == kF16) return launch_spw<kF16, 1>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
+  return launch_spw<kBF16, 1>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
 }
 
 // ------------------------------------------------------------------ repack

@@ -141,8 +141,7 @@ __device__ __forceinline__ void cluster_sync() {
 }
 // Arrive on an mbarrier that may live in another CTA of the cluster.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // Pair-CTA tile load (no multicast): data lands in this CTA's shared memory,
 // the transaction bytes are counted on the leader CTA's mbarrier.
@@ -205,6 +204,17 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr) {
                    cluster_addr)
                : "memory");
 }
+// One commit whose arrival lands on the same barrier offset in both CTAs of
+// the pair (ctaMask 0b11).  This is a tcgen05 completion signal, not a
+// memory load.
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t local_addr) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], m;\n\t}" ::"r"(local_addr)
+      : "memory");
+}
+
 template <int KIND>
 __device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                           uint32_t idesc, uint32_t accumulate) {

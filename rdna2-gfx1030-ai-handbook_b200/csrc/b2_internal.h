@@ -30,6 +30,7 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
 
 // 0 = automatic, 1 = single-CTA kernel only, 2 = 2-CTA pair kernel only.
 void set_gemm_path(int path);
+int pair_capacity();
 
 // Per-row rotate + quantize (quant 0 = int8 /127, 1 = e4m3 /448).
 cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,

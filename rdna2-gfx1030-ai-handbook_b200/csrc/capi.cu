@@ -82,8 +82,10 @@ const char* b2_error_string(int status) { return cudaGetErrorString(static_cast<
 
 int b2_sm_count(void) { return b2::device_sm_count(); }
 
+int b2_pair_capacity(void) { return b2::pair_capacity(); }
+
 int b2_set_gemm_path(int path) {
-  if (path < 0 || path > 2) return fail();
+  if (path < 0 || path > 6) return fail();
   b2::set_gemm_path(path);
   return 0;
 }

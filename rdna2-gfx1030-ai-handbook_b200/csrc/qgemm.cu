@@ -45,7 +45,8 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
 
-// Shared-memory plan: A ring, B ring, per-warp epilogue scale/bias, barriers.
+// Shared-memory plan: A ring, B ring, per-warp staging of one 32-column chunk
+// of epilogue scale/bias, barriers.
 template <int A_ROWS, int B_ROWS, int BN, int STAGES>
 struct Smem {
   static constexpr int kABytes = A_ROWS * 128;
@@ -54,7 +55,7 @@ struct Smem {
   static constexpr int kOffA = 0;
   static constexpr int kOffB = STAGES * kABytes;
   static constexpr int kOffEpi = STAGES * kStageBytes;
-  static constexpr int kOffBar = kOffEpi + kEpiWarps * 2 * BN * 4;
+  static constexpr int kOffBar = kOffEpi + kEpiWarps * 64 * 4;
   static constexpr int kNumBars = 2 * STAGES + 4;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   static constexpr int kBytes = kOffMisc + 16;
@@ -174,45 +175,51 @@ __device__ __forceinline__ void store_dispatch(const GemmParams& p, const uint32
   }
 }
 
-// Epilogue of one accumulator tile by one warp (32 rows x BN columns).
+// Per-lane scale and bias of column n (Kitchen mode pre-rounds the bias
+// through the output dtype, as `bias.to(out_dtype)` does).
+__device__ __forceinline__ void load_col(const GemmParams& p, int n, float sb0, float& sb, float& b) {
+  sb = sb0;
+  b = 0.0f;
+  if (n < p.N) {
+    if (p.sb != nullptr && !p.sb_scalar) sb = p.sb[n];
+    if (p.bias != nullptr) {
+      b = load_as_float(p.bias, p.bias_dtype, n);
+      if (p.epilogue == kEpiKitchen) {
+        if (p.out_dtype == kF16) b = round_through<kF16>(b);
+        if (p.out_dtype == kBF16) b = round_through<kBF16>(b);
+      }
+    }
+  }
+}
+
+// Epilogue of one accumulator tile by one warp (32 rows x BN columns), one
+// 32-column chunk at a time.  TMEM loads are double buffered (chunk c+1 in
+// flight while chunk c is converted and stored) and the next chunk's scale
+// and bias are fetched into registers while the current chunk is stored.
 // `release` runs once every TMEM read of the tile has completed.
 template <int KIND, int BN, typename Release>
 __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t taddr, int row, int n0,
-                                              int lane, float* wsb, Release release) {
+                                              int lane, float* wst, Release release) {
   constexpr int NC = BN / 32;
   static_assert(NC % 2 == 0, "ping-pong over chunk pairs");
-  float* wbias = wsb + BN;
-  // Stage this tile's per-channel scale and bias in the warp's own slice.
-  __syncwarp();
   const float sb0 = (p.sb != nullptr && p.sb_scalar) ? p.sb[0] : 0.0f;
-#pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const int n = n0 + c * 32 + lane;
-    float sb = sb0, b = 0.0f;
-    if (n < p.N) {
-      if (p.sb != nullptr && !p.sb_scalar) sb = p.sb[n];
-      if (p.bias != nullptr) {
-        b = load_as_float(p.bias, p.bias_dtype, n);
-        if (p.epilogue == kEpiKitchen) {
-          if (p.out_dtype == kF16) b = round_through<kF16>(b);
-          if (p.out_dtype == kBF16) b = round_through<kBF16>(b);
-        }
-      }
-    }
-    wsb[c * 32 + lane] = sb;
-    wbias[c * 32 + lane] = b;
-  }
-  __syncwarp();
   const float sa = (p.sa != nullptr && row < p.M) ? p.sa[row] : 0.0f;
+  float sb_n, b_n;
+  load_col(p, n0 + lane, sb0, sb_n, b_n);
   uint32_t r0[32], r1[32];
   __syncwarp();
   tmem_ld32(taddr, r0);
   tmem_ld_wait(r0);
 #pragma unroll 1
   for (int c = 0; c < NC; c += 2) {
+    // chunk c (in r0)
     __syncwarp();
+    wst[lane] = sb_n;
+    wst[32 + lane] = b_n;
+    __syncwarp();
+    load_col(p, n0 + (c + 1) * 32 + lane, sb0, sb_n, b_n);
     tmem_ld32(taddr + static_cast<uint32_t>((c + 1) * 32), r1);
-    store_dispatch<KIND>(p, r0, row, n0 + c * 32, sa, wsb + c * 32, wbias + c * 32);
+    store_dispatch<KIND>(p, r0, row, n0 + c * 32, sa, wst, wst + 32);
     __syncwarp();
     tmem_ld_wait(r1);
     if (c + 2 < NC) {
@@ -220,8 +227,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tadd
     } else {
       release();  // all TMEM reads of this tile are complete
     }
-    store_dispatch<KIND>(p, r1, row, n0 + (c + 1) * 32, sa, wsb + (c + 1) * 32,
-                         wbias + (c + 1) * 32);
+    // chunk c+1 (in r1)
+    __syncwarp();
+    wst[lane] = sb_n;
+    wst[32 + lane] = b_n;
+    __syncwarp();
+    if (c + 2 < NC) load_col(p, n0 + (c + 2) * 32 + lane, sb0, sb_n, b_n);
+    store_dispatch<KIND>(p, r1, row, n0 + (c + 1) * 32, sa, wst, wst + 32);
     __syncwarp();
     if (c + 2 < NC) tmem_ld_wait(r0);
   }
@@ -344,7 +356,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int quarter = warp & 3;  // TMEM lanes this warp may access
-    float* wsb = reinterpret_cast<float*>(smem + L::kOffEpi) + (warp - 2) * 2 * BN;
+    float* wsb = reinterpret_cast<float*>(smem + L::kOffEpi) + (warp - 2) * 64;
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int buf = t & 1;
@@ -377,8 +389,9 @@ __global__ void __launch_bounds__(192, 1)
 // [128r, 128r+128) and B rows [r*BN/2, (r+1)*BN/2) of every k-block and
 // accumulates its 128 x BN half in its own TMEM.  The leader (rank 0) waits
 // on its `full` barrier (both CTAs' loads count there), issues the pair MMAs
-// and commits to both CTAs' `empty` / `tfull` barriers; both epilogues hand
-// TMEM back through the leader's `tempty` barrier (8 arrivals).
+// and signals both CTAs' `empty` / `tfull` barriers with one commit each;
+// both epilogues hand TMEM back through the leader's `tempty` barrier (8
+// arrivals).
 template <int KIND, int BN, int STAGES>
 __global__ void __launch_bounds__(192, 1)
     qgemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
@@ -454,7 +467,7 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       }
-      // Tail: every slot released by the leader's commits before exit.
+      // Tail: every slot released (and forwarded) before exit.
       for (int i = 0; i < STAGES && ok; ++i) {
         ok = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer);
         if (++stage == STAGES) {
@@ -466,8 +479,6 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 1) {
     if (leader && lane == 0) {
       constexpr uint32_t idesc = make_idesc<KIND>(256, BN);
-      const uint32_t peer_empty = mapa_shared(smem_u32(&empty[0]), 1);
-      const uint32_t peer_tfull = mapa_shared(smem_u32(&tfull[0]), 1);
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -483,28 +494,28 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
             break;
           }
-          tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + L::kOffA + stage * L::kABytes);
           const uint32_t b_addr = smem_u32(smem + L::kOffB + stage * L::kBBytes);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_pair<KIND>(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32),
                             idesc, (kb | kk) != 0 ? 1u : 0u);
-          umma_commit_pair(smem_u32(&empty[stage]));
-          umma_commit_pair(peer_empty + static_cast<uint32_t>(stage * 8));
+          // One completion signal to both CTAs' `empty[stage]` barriers.
+          umma_commit_pair_both(smem_u32(&empty[stage]));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
+          // Peek at the next stage so its wait overlaps the MMAs just issued.
+          if (kb + 1 < p.num_kb) mbar_try_wait(&full[stage], phase);
         }
         if (!ok) break;
-        umma_commit_pair(smem_u32(&tfull[buf]));
-        umma_commit_pair(peer_tfull + static_cast<uint32_t>(buf * 8));
+        umma_commit_pair_both(smem_u32(&tfull[buf]));
       }
     }
   } else {
     const int quarter = warp & 3;
-    float* wsb = reinterpret_cast<float*>(smem + L::kOffEpi) + (warp - 2) * 2 * BN;
+    float* wsb = reinterpret_cast<float*>(smem + L::kOffEpi) + (warp - 2) * 64;
     const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
     int t = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++t) {
@@ -670,26 +681,70 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-// Wave-quantization aware N tile for the pair kernel: among 256 and 192
-// choose the one whose persistent waves are fullest.
-static int choose_pair_bn(int64_t M, int64_t N, int pairs) {
-  const int64_t tm = (M + 255) / 256;
-  double best = -1.0;
-  int bn = 256;
-  for (int cand : {256, 192}) {
-    const int64_t tiles = tm * ((N + cand - 1) / cand);
-    const int64_t waves = (tiles + pairs - 1) / pairs;
-    const double eff = static_cast<double>(tiles) / static_cast<double>(waves * pairs) *
-                       (cand == 256 ? 1.0 : 0.97);
-    if (eff > best + 1e-9) {
-      best = eff;
-      bn = cand;
-    }
+// Co-resident 2-CTA clusters of the pair kernel on the current device (the
+// persistent grid size in pairs), or -1 when cluster launch is unavailable.
+int pair_capacity() {
+  using L = Smem<128, 128, 256, 6>;
+  auto kernel = qgemm_pair_kernel<kKindI8, 256, 6>;
+  static bool configured[64] = {false};
+  static int cap[64] = {0};
+  const int dev = current_device();
+  if (dev >= 64) return -1;
+  if (cap[dev] != 0) return cap[dev];
+  if (configure_once(kernel, L::kAlloc, configured) != cudaSuccess) {
+    cudaGetLastError();
+    return cap[dev] = -1;
   }
-  return bn;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2 * (device_sm_count() / 2));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    n = -1;
+  }
+  return cap[dev] = n;
 }
 
-static int g_force_path = 0;  // 0 auto, 1 single-CTA only, 2 pair only
+// Choose between 128x256 single-CTA tiles and 256x256 pair tiles by the
+// modelled time of their persistent waves; pair tiles cost ~5% less per
+// MAC (half the B operand per SM from shared memory and L2).
+static int choose_config(int64_t M, int64_t N) {
+  const int64_t tn = (N + 255) / 256;
+  const int64_t t1 = (M + 127) / 128 * tn;
+  const int64_t w1 = (t1 + device_sm_count() - 1) / device_sm_count();
+  const int pairs = pair_capacity();
+  if (N <= 128 && M <= 128) return 4;
+  if (pairs <= 0 || M <= 128) return N <= 128 ? 4 : 3;
+  const int64_t t2 = (M + 255) / 256 * tn;
+  const int64_t w2 = (t2 + pairs - 1) / pairs;
+  // one pair wave does twice a single wave's rows in the same time
+  return static_cast<double>(w2) * 0.95 < static_cast<double>(w1) ? 5 : 3;
+}
+
+// Kernel selection: 0 auto; 1 single-CTA (auto N tile); 2 pair (auto N tile);
+// 3 single BN=256; 4 single BN=128; 5 pair BN=256; 6 pair BN=192.
+static int g_force_path = 0;
+
+template <int KIND>
+static cudaError_t dispatch(int cfg, const void* a, int64_t lda, const void* b, int64_t ldb,
+                           const GemmParams& p, int max_ctas, cudaStream_t stream) {
+  switch (cfg) {
+    case 3: return launch_single<KIND, 256, 4>(a, lda, b, ldb, p, max_ctas, stream);
+    case 4: return launch_single<KIND, 128, 6>(a, lda, b, ldb, p, max_ctas, stream);
+    case 5: return launch_pair<KIND, 256, 6>(a, lda, b, ldb, p, max_ctas, stream);
+    case 6: return launch_pair<KIND, 192, 7>(a, lda, b, ldb, p, max_ctas, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
 
 cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams p,
                       int max_ctas, cudaStream_t stream) {
@@ -697,32 +752,22 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
   const int eb = kind == kKindBF16 ? 2 : 1;
   const int kb_elems = 128 / eb;
   p.num_kb = static_cast<int>((p.K + kb_elems - 1) / kb_elems);
-  const bool pair = g_force_path == 2 || (g_force_path == 0 && p.M > 128);
-  if (pair) {
-    const int bn = choose_pair_bn(p.M, p.N, device_sm_count() / 2);
-    cudaError_t e;
-    if (kind == kKindI8)
-      e = bn == 256 ? launch_pair<kKindI8, 256, 6>(a, lda, b, ldb, p, max_ctas, stream)
-                    : launch_pair<kKindI8, 192, 7>(a, lda, b, ldb, p, max_ctas, stream);
-    else if (kind == kKindE4M3)
-      e = bn == 256 ? launch_pair<kKindE4M3, 256, 6>(a, lda, b, ldb, p, max_ctas, stream)
-                    : launch_pair<kKindE4M3, 192, 7>(a, lda, b, ldb, p, max_ctas, stream);
-    else
-      e = bn == 256 ? launch_pair<kKindBF16, 256, 6>(a, lda, b, ldb, p, max_ctas, stream)
-                    : launch_pair<kKindBF16, 192, 7>(a, lda, b, ldb, p, max_ctas, stream);
-    if (e != cudaErrorNotSupported || g_force_path == 2) return e;
-  }
-  // Single-CTA tiles: 256 wide when that still fills the machine, else 128.
+  int cfg = g_force_path;
   const int64_t tm = (p.M + 127) / 128;
-  const bool wide = p.N > 128 && tm * ((p.N + 255) / 256) >= device_sm_count();
-  if (kind == kKindI8)
-    return wide ? launch_single<kKindI8, 256, 4>(a, lda, b, ldb, p, max_ctas, stream)
-                : launch_single<kKindI8, 128, 6>(a, lda, b, ldb, p, max_ctas, stream);
-  if (kind == kKindE4M3)
-    return wide ? launch_single<kKindE4M3, 256, 4>(a, lda, b, ldb, p, max_ctas, stream)
-                : launch_single<kKindE4M3, 128, 6>(a, lda, b, ldb, p, max_ctas, stream);
-  return wide ? launch_single<kKindBF16, 256, 4>(a, lda, b, ldb, p, max_ctas, stream)
-              : launch_single<kKindBF16, 128, 6>(a, lda, b, ldb, p, max_ctas, stream);
+  const bool wide = p.N > 128 && tm * ((p.N + 255) / 256) >= device_sm_count() / 2;
+  if (cfg == 0) cfg = choose_config(p.M, p.N);
+  if (cfg == 2) cfg = 5;
+  if (cfg == 1) cfg = wide ? 3 : 4;
+  cudaError_t e = kind == kKindI8     ? dispatch<kKindI8>(cfg, a, lda, b, ldb, p, max_ctas, stream)
+                  : kind == kKindE4M3 ? dispatch<kKindE4M3>(cfg, a, lda, b, ldb, p, max_ctas, stream)
+                                      : dispatch<kKindBF16>(cfg, a, lda, b, ldb, p, max_ctas, stream);
+  if (e == cudaErrorNotSupported && cfg >= 5 && g_force_path == 0) {
+    cfg = wide ? 3 : 4;  // cluster launch unavailable: single-CTA tiles
+    e = kind == kKindI8     ? dispatch<kKindI8>(cfg, a, lda, b, ldb, p, max_ctas, stream)
+        : kind == kKindE4M3 ? dispatch<kKindE4M3>(cfg, a, lda, b, ldb, p, max_ctas, stream)
+                            : dispatch<kKindBF16>(cfg, a, lda, b, ldb, p, max_ctas, stream);
+  }
+  return e;
 }
 
 void set_gemm_path(int path) { g_force_path = path; }

@@ -32,9 +32,11 @@ FLOAT_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 
 def set_gemm_path(path):
     """Process-wide GEMM kernel choice: "auto", "single" (1-CTA 128-row
-    tiles) or "pair" (2-CTA cta_group::2 256-row tiles).  Results are
+    tiles), "pair" (2-CTA cta_group::2 256-row tiles), or a fixed tile:
+    "single256", "single128", "pair256", "pair192".  Results are
     bit-identical; this is a tuning and verification knob."""
-    code = {"auto": 0, "single": 1, "pair": 2}[path]
+    code = {"auto": 0, "single": 1, "pair": 2, "single256": 3, "single128": 4, "pair256": 5,
+            "pair192": 6}[path]
     nat.check(nat.library().b2_set_gemm_path(code), "b2_set_gemm_path")
 
 
