@@ -114,6 +114,26 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
                     void* out, int out_dtype, int64_t ldc, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Allocation-free fused quantized linear: the same computation and results
+ * as b2_quant_linear, for callers that cannot provide a workspace (a host
+ * whose device memory is all owned by another allocator, a plugin calling
+ * convention that carries only inputs and outputs, or code that must not call
+ * cudaMalloc because it can synchronize the device).  The staging buffer is a
+ * fixed device array inside the library: every GPU that loads the library
+ * holds b2_quant_linear_noalloc_max_bytes() bytes for it until exit, a call
+ * needing more staging (b2_quant_linear_workspace_bytes(M, K)) is rejected
+ * with cudaErrorInvalidValue, and calls that overlap on the GPU share the
+ * array and race -- keep them on one stream.  The first call on a device looks
+ * up the array's address; make it before any stream capture.  Allocates
+ * nothing.  No counterpart in the reference (its operators always allocate
+ * their outputs through PyTorch). */
+size_t b2_quant_linear_noalloc_max_bytes(void);
+int b2_quant_linear_noalloc(int kind, const void* x, int x_dtype, int64_t M, int64_t K,
+                            int64_t ldx, int block, const void* w, int64_t ldw, int64_t N,
+                            const float* w_scale, int64_t w_scale_count, const void* bias,
+                            int bias_dtype, int epilogue, void* out, int out_dtype, int64_t ldc,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -40,6 +40,9 @@ SIGNATURES = {
     "b2_quant_linear_workspace_bytes": ([_i64, _i64], _size),
     "b2_quant_linear": ([_int, _p, _int, _i64, _i64, _i64, _int, _p, _i64, _i64, _p, _i64, _p,
                          _int, _int, _p, _int, _i64, _p, _size, _p], _int),
+    "b2_quant_linear_noalloc_max_bytes": ([], _size),
+    "b2_quant_linear_noalloc": ([_int, _p, _int, _i64, _i64, _i64, _int, _p, _i64, _i64, _p, _i64,
+                                 _p, _int, _int, _p, _int, _i64, _p], _int),
 }
 
 
