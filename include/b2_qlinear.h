@@ -21,6 +21,7 @@
  * kind:         0 = int8 x int8 -> int32 (tcgen05 kind::i8)
  *               1 = e4m3 x e4m3 -> fp32  (tcgen05 kind::f8f6f4)
  *               2 = bf16 x bf16 -> fp32  (tcgen05 kind::f16)
+ *               3 = fp16 x fp16 -> fp32  (tcgen05 kind::f16)
  */
 #ifndef B2_QLINEAR_H_
 #define B2_QLINEAR_H_
@@ -113,6 +114,44 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
                     int64_t w_scale_count, const void* bias, int bias_dtype, int epilogue,
                     void* out, int out_dtype, int64_t ldc, void* workspace,
                     size_t workspace_bytes, void* stream);
+
+/* Split-K workspace bytes b2_w4a16_gemm needs for these sizes (0 = none). */
+size_t b2_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K);
+
+/* W4A16 weight-only GEMM: out[m,n] = sum_k a[m,k] * w[n,k] (+ bias[n]) with
+ * w[n,k] = round((u - zu) * s) in the activation's 16-bit type.
+ *   a       [M,K] fp16 (a_dtype 1) or bf16 (2), row stride lda, 16-byte rows
+ *   wq      [N, ldw] int32 words, unsigned nibble k at bits 4*(k%8) of word k/8
+ *   scales, zeros  [N, ldsz] in a_dtype; zeros are the integers zu in [0,15]
+ *   group   32, 64 or 128; K a multiple of 64 and of group
+ *   out     [M,N] in a_dtype, row stride ldo
+ *   workspace >= b2_w4a16_workspace_bytes(M, N, K) (split-K partials)
+ * Replaces int4_linear_a16 / _linear_dot2 (rdna2_ops/int4_weight_gemm_v07.py
+ * :540-564, 365-387) in the north-star uint4 + 16-bit scale/zero format. */
+int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* wq, int64_t ldw,
+                  const void* scales, const void* zeros, int64_t ldsz, int group, int64_t M,
+                  int64_t N, int64_t K, const void* bias, int bias_dtype, void* out, int64_t ldo,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* dst = src ^ 0x88888888 over n_words words: converts the reference's signed
+ * nibbles (q = u - 8, PackedInt4 at int4_weight_gemm_v07.py:20-46) to the
+ * unsigned nibbles b2_w4a16_gemm reads, and back. */
+int b2_int4_flip_nibbles(const void* src, void* dst, int64_t n_words, void* stream);
+
+/* Group INT4 packer with the semantics of pack_int4 / pack_int4_cpu
+ * (rdna2_ops/int4_weight_gemm_v07.py:49-82, 413-430): w [N,K] of w_dtype
+ * (0/1/2), row stride ldw; outputs PackedInt4 storage -- data int32 words
+ * (layout_kn 0: [N,K/8], 1: [K/8,N]; order_high puts element 0 in the top
+ * nibble), scales fp32 [N,K/group], zeros int32 (zu - 8), sums int32. */
+int b2_pack_int4(const void* w, int w_dtype, int64_t ldw, int64_t N, int64_t K, int group,
+                 int symmetric, int layout_kn, int order_high, void* data, float* scales,
+                 void* zeros, void* sums, void* stream);
+
+/* Decode PackedInt4 storage (rdna2_ops/int4_weight_gemm_v07.py:433-441):
+ * out_dtype 0 = fp32 (q - z) * s, 1 = fp16 of the same, 3 = int8 q - z. */
+int b2_unpack_int4(const void* data, int layout_kn, int order_high, const float* scales,
+                   const void* zeros, int64_t N, int64_t K, int group, int out_dtype, void* out,
+                   void* stream);
 
 /* Allocation-free fused quantized linear: the same computation and results
  * as b2_quant_linear, for callers that cannot provide a workspace (a host

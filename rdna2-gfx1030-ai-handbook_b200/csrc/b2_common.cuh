@@ -14,20 +14,17 @@ namespace b2 {
 // dtype codes shared with include/b2_qlinear.h
 enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2, kI32 = 3 };
 enum Epilogue : int { kEpiSeparate = 0, kEpiFma = 1, kEpiKitchen = 2, kEpiNone = 3 };
-enum Kind : int { kKindI8 = 0, kKindE4M3 = 1, kKindBF16 = 2 };
+enum Kind : int { kKindI8 = 0, kKindE4M3 = 1, kKindBF16 = 2, kKindF16 = 3 };
 
-// Device status word written when a bounded wait gives up.  Encoding:
-// 0 = ok, otherwise 0x100 | site (see kSite* below).  Read via b2_device_status.
-// Defined in the translation unit that owns the kernels with bounded waits
-// (qgemm.cu, which also hosts b2_device_status); other units never touch it.
-#ifdef B2_STATUS_OWNER
-__device__ int g_b2_status = 0;
-#endif
+// Device status word written when a bounded wait gives up: 0 = ok,
+// otherwise 0x100 | site (kSite* below).  It lives in qgemm.cu; kernels get
+// its device address (status_word_ptr()) and b2_device_status reads it.
 enum : int {
   kSiteProducer = 1,
   kSiteMma = 2,
   kSiteMmaTmem = 3,
   kSiteEpilogue = 4,
+  kSiteTransform = 5,
 };
 
 // Longest time any single mbarrier wait may take before the CTA abandons its
@@ -75,12 +72,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-#ifdef B2_STATUS_OWNER
 // Bounded wait.  Returns false (and raises the CTA abort flag plus the device
 // status word) when the phase does not complete within kWaitLimitNs, or when
 // another role of this CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int site) {
+                                          int site, int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer();
   for (uint32_t i = 1;; ++i) {
@@ -89,13 +85,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       if (*abort_flag) return false;
       if (globaltimer() - start > kWaitLimitNs) {
         *abort_flag = 1;
-        atomicCAS(&g_b2_status, 0, 0x100 | site);
+        if (status != nullptr) atomicCAS(status, 0, 0x100 | site);
         return false;
       }
     }
   }
 }
-#endif  // B2_STATUS_OWNER
 
 // ----------------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
@@ -264,6 +259,7 @@ template <int KIND>
 __host__ __device__ constexpr uint32_t make_idesc(int m, int n) {
   return (KIND == kKindI8 ? (2u << 4) | (1u << 7) | (1u << 10)      // S32 acc, signed int8
           : KIND == kKindE4M3 ? (1u << 4)                          // F32 acc, E4M3 x E4M3
+          : KIND == kKindF16  ? (1u << 4)                          // F32 acc, F16 x F16
                               : (1u << 4) | (1u << 7) | (1u << 10)) // F32 acc, BF16 x BF16
          | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(m >> 4) << 24);
 }

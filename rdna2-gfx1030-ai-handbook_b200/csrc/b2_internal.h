@@ -19,7 +19,11 @@ struct GemmParams {
   int64_t ldc;         // output row stride in elements
   int epilogue;
   int vec_ok;          // output rows 16-byte aligned: vector stores allowed
+  int* status;         // device status word for bounded waits
 };
+
+// Device address of the bounded-wait status word on the current device.
+int* status_word_ptr();
 
 int device_sm_count();
 
@@ -40,5 +44,20 @@ cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int6
 // dst[r, c] = src[r*s_row + c*s_col] for c < cols, 0 for cols <= c < ldd.
 cudaError_t run_repack(const void* src, int elem_bytes, int64_t rows, int64_t cols, int64_t s_row,
                        int64_t s_col, void* dst, int64_t ldd, cudaStream_t stream);
+
+// W4A16 (see w4a16.cu); `partial` holds splits * M * N fp32 when splits > 1.
+cudaError_t run_w4a16(const void* a, int a_dtype, int64_t lda, const uint32_t* wq, int64_t ldw,
+                      const uint16_t* scales, const uint16_t* zeros, int64_t ldsz, int group,
+                      int64_t M, int64_t N, int64_t K, const void* bias, int bias_dtype, void* out,
+                      int64_t ldo, float* partial, size_t partial_bytes, int splits,
+                      cudaStream_t stream);
+int w4a16_splits(int64_t M, int64_t N, int64_t K);
+cudaError_t run_nibble_flip(const uint32_t* src, uint32_t* dst, int64_t n, cudaStream_t stream);
+cudaError_t run_pack_int4(const void* w, int w_dtype, int64_t ldw_el, int64_t N, int64_t K, int G,
+                          int symmetric, int layout_kn, int order_high, int32_t* data, float* scales,
+                          int32_t* zeros, int32_t* sums, cudaStream_t stream);
+cudaError_t run_unpack_int4(const int32_t* data, int layout_kn, int order_high, const float* scales,
+                            const int32_t* zeros, int64_t N, int64_t K, int G, int out_dtype, void* out,
+                            cudaStream_t stream);
 
 }  // namespace b2

@@ -23,13 +23,13 @@ bool valid_block(int block, int64_t K) {
   return K % block == 0;
 }
 
-int elem_bytes(int kind) { return kind == b2::kKindBF16 ? 2 : 1; }
+int elem_bytes(int kind) { return (kind == b2::kKindBF16 || kind == b2::kKindF16) ? 2 : 1; }
 
 int check_gemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N,
                int64_t K, const float* a_scale, const float* b_scale, int64_t b_scale_count,
                const void* bias, int bias_dtype, int epilogue, const void* out, int out_dtype,
                int64_t ldc) {
-  if (kind < 0 || kind > 2) return fail();
+  if (kind < 0 || kind > 3) return fail();
   if (M < 0 || N < 0 || K < 1 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail();
   if (kind == b2::kKindI8 && K > 131071) return fail();  // INT32 accumulator bound
   if (M == 0 || N == 0) return 0;
@@ -152,6 +152,71 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
   b2::GemmParams p = make_params(M, N, K, sa, w_scale, w_scale_count, bias, bias_dtype, epilogue,
                                  out, out_dtype, ldc);
   return static_cast<int>(b2::run_qgemm(kind, q, ldq, w, ldw, p, 0, s));
+}
+
+size_t b2_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0 || N <= 0 || K < 64) return 0;
+  const int splits = b2::w4a16_splits(M, N, K);
+  return splits > 1 ? static_cast<size_t>(splits) * M * N * 4 : 0;
+}
+
+int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* wq, int64_t ldw,
+                  const void* scales, const void* zeros, int64_t ldsz, int group, int64_t M, int64_t N,
+                  int64_t K, const void* bias, int bias_dtype, void* out, int64_t ldo, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (a_dtype != b2::kF16 && a_dtype != b2::kBF16) return fail();
+  if (M < 0 || N < 0 || K < 64 || K % 64 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail();
+  if (group != 32 && group != 64 && group != 128) return fail();
+  if (K % group) return fail();
+  if (M == 0 || N == 0) return 0;
+  if (!a || !wq || !scales || !zeros || !out) return fail();
+  if (!aligned16(a) || (lda * 2) % 16 || lda < K) return fail();
+  if (!aligned16(wq) || (ldw * 4) % 16 || ldw < K / 8) return fail();
+  if (ldsz < K / group || ldo < N) return fail();
+  if (bias && (bias_dtype < 0 || bias_dtype > 2)) return fail();
+  const int splits = b2::w4a16_splits(M, N, K);
+  if (splits > 1 && (workspace == nullptr || workspace_bytes < static_cast<size_t>(splits) * M * N * 4))
+    return fail();
+  return static_cast<int>(b2::run_w4a16(a, a_dtype, lda, static_cast<const uint32_t*>(wq), ldw,
+                                        static_cast<const uint16_t*>(scales),
+                                        static_cast<const uint16_t*>(zeros), ldsz, group, M, N, K, bias,
+                                        bias_dtype, out, ldo, static_cast<float*>(workspace),
+                                        workspace_bytes, splits, static_cast<cudaStream_t>(stream)));
+}
+
+int b2_int4_flip_nibbles(const void* src, void* dst, int64_t n_words, void* stream) {
+  if (n_words < 0) return fail();
+  if (n_words == 0) return 0;
+  if (!src || !dst) return fail();
+  return static_cast<int>(b2::run_nibble_flip(static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst),
+                                              n_words, static_cast<cudaStream_t>(stream)));
+}
+
+int b2_pack_int4(const void* w, int w_dtype, int64_t ldw, int64_t N, int64_t K, int group, int symmetric,
+                 int layout_kn, int order_high, void* data, float* scales, void* zeros, void* sums,
+                 void* stream) {
+  if (w_dtype < 0 || w_dtype > 2 || N < 0 || K < 0 || N > INT32_MAX || K > INT32_MAX) return fail();
+  if (group != 32 && group != 64 && group != 128) return fail();
+  if (K % group || ldw < K) return fail();
+  if (N == 0 || K == 0) return 0;
+  if (!w || !data || !scales || !zeros || !sums) return fail();
+  return static_cast<int>(b2::run_pack_int4(w, w_dtype, ldw, N, K, group, symmetric != 0, layout_kn != 0,
+                                            order_high != 0, static_cast<int32_t*>(data), scales,
+                                            static_cast<int32_t*>(zeros), static_cast<int32_t*>(sums),
+                                            static_cast<cudaStream_t>(stream)));
+}
+
+int b2_unpack_int4(const void* data, int layout_kn, int order_high, const float* scales, const void* zeros,
+                   int64_t N, int64_t K, int group, int out_dtype, void* out, void* stream) {
+  if (N < 0 || K < 0 || N > INT32_MAX || K > INT32_MAX) return fail();
+  if (group != 32 && group != 64 && group != 128) return fail();
+  if (K % group) return fail();
+  if (out_dtype != b2::kF32 && out_dtype != b2::kF16 && out_dtype != 3) return fail();
+  if (N == 0 || K == 0) return 0;
+  if (!data || !zeros || !out || (out_dtype != 3 && !scales)) return fail();
+  return static_cast<int>(b2::run_unpack_int4(static_cast<const int32_t*>(data), layout_kn != 0,
+                                              order_high != 0, scales, static_cast<const int32_t*>(zeros),
+                                              N, K, group, out_dtype, out, static_cast<cudaStream_t>(stream)));
 }
 
 }  // extern "C"

@@ -33,11 +33,27 @@
 //   none      raw INT32 accumulator              (int8_matmul, :195-200)
 #include <mutex>
 
-#define B2_STATUS_OWNER 1
 #include "b2_common.cuh"
 #include "b2_internal.h"
 
 namespace b2 {
+
+__device__ int g_b2_status = 0;
+
+int* status_word_ptr() {
+  static int* cache[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cache[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_b2_status) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    cache[dev] = static_cast<int*>(p);
+  }
+  return cache[dev];
+}
 
 constexpr int kEpiWarps = 4;
 
@@ -245,7 +261,7 @@ __global__ void __launch_bounds__(192, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  const GemmParams p) {
   using L = Smem<128, BN, BN, STAGES>;
-  constexpr int kKbElems = (KIND == kKindBF16) ? 64 : 128;  // 128 bytes of K per k-block
+  constexpr int kKbElems = (KIND == kKindBF16 || KIND == kKindF16) ? 64 : 128;  // 128 bytes of K per k-block
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -294,7 +310,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer)) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status)) {
             ok = false;
             break;
           }
@@ -312,7 +328,7 @@ __global__ void __launch_bounds__(192, 1)
       // Tail: wait until the MMA warp has released every slot, so no commit
       // is still in flight to this CTA's barriers when it exits.
       for (int i = 0; i < STAGES && ok; ++i) {
-        ok = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer);
+        ok = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status);
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -329,11 +345,11 @@ __global__ void __launch_bounds__(192, 1)
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
         const int buf = t & 1;
         const uint32_t use = static_cast<uint32_t>(t >> 1);
-        if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag, kSiteMmaTmem)) break;
+        if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag, kSiteMmaTmem, p.status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteMma)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteMma, p.status)) {
             ok = false;
             break;
           }
@@ -362,7 +378,7 @@ __global__ void __launch_bounds__(192, 1)
       const int buf = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
       const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
-      bool ok = mbar_wait(&tfull[buf], use & 1u, abort_flag, kSiteEpilogue);
+      bool ok = mbar_wait(&tfull[buf], use & 1u, abort_flag, kSiteEpilogue, p.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
@@ -397,7 +413,7 @@ __global__ void __launch_bounds__(192, 1)
     qgemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                       const __grid_constant__ CUtensorMap tma_b, const GemmParams p) {
   using L = Smem<128, BN / 2, BN, STAGES>;
-  constexpr int kKbElems = (KIND == kKindBF16) ? 64 : 128;
+  constexpr int kKbElems = (KIND == kKindBF16 || KIND == kKindF16) ? 64 : 128;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -451,7 +467,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
         const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer)) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status)) {
             ok = false;
             break;
           }
@@ -469,7 +485,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       // Tail: every slot released (and forwarded) before exit.
       for (int i = 0; i < STAGES && ok; ++i) {
-        ok = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer);
+        ok = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status);
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -486,11 +502,11 @@ __global__ void __launch_bounds__(192, 1)
       for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++t) {
         const int buf = t & 1;
         const uint32_t use = static_cast<uint32_t>(t >> 1);
-        if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag, kSiteMmaTmem)) break;
+        if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag, kSiteMmaTmem, p.status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteMma)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteMma, p.status)) {
             ok = false;
             break;
           }
@@ -522,7 +538,7 @@ __global__ void __launch_bounds__(192, 1)
       const int buf = t & 1;
       const uint32_t use = static_cast<uint32_t>(t >> 1);
       const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
-      bool ok = mbar_wait(&tfull[buf], use & 1u, abort_flag, kSiteEpilogue);
+      bool ok = mbar_wait(&tfull[buf], use & 1u, abort_flag, kSiteEpilogue, p.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
@@ -565,6 +581,8 @@ static EncodeTiledFn encoder() {
   });
   return fn;
 }
+
+EncodeTiledFn tensor_map_encoder() { return encoder(); }
 
 // 2-D K-major operand map: dims {inner (K elements), rows}, 128-byte swizzle,
 // box {128 bytes of K, box_rows}; out-of-range elements read as zero.
@@ -621,7 +639,7 @@ static cudaError_t launch_single(const void* a, int64_t lda, const void* b, int6
   static bool configured[64] = {false};
   cudaError_t e = configure_once(kernel, L::kAlloc, configured);
   if (e != cudaSuccess) return e;
-  const int eb = KIND == kKindBF16 ? 2 : 1;
+  const int eb = (KIND == kKindBF16 || KIND == kKindF16) ? 2 : 1;
   CUtensorMap ma, mb;
   if ((e = make_kmajor_map(&ma, a, eb, p.K, p.M, lda * eb, 128)) != cudaSuccess) return e;
   if ((e = make_kmajor_map(&mb, b, eb, p.K, p.N, ldb * eb, BN)) != cudaSuccess) return e;
@@ -666,7 +684,7 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
     max_pairs[dev] = n;
   }
   if (max_pairs[dev] < 0) return cudaErrorNotSupported;
-  const int eb = KIND == kKindBF16 ? 2 : 1;
+  const int eb = (KIND == kKindBF16 || KIND == kKindF16) ? 2 : 1;
   CUtensorMap ma, mb;
   if ((e = make_kmajor_map(&ma, a, eb, p.K, p.M, lda * eb, 128)) != cudaSuccess) return e;
   if ((e = make_kmajor_map(&mb, b, eb, p.K, p.N, ldb * eb, BN / 2)) != cudaSuccess) return e;
@@ -749,7 +767,8 @@ static cudaError_t dispatch(int cfg, const void* a, int64_t lda, const void* b, 
 cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams p,
                       int max_ctas, cudaStream_t stream) {
   if (p.M == 0 || p.N == 0) return cudaSuccess;
-  const int eb = kind == kKindBF16 ? 2 : 1;
+  p.status = status_word_ptr();
+  const int eb = (kind == kKindBF16 || kind == kKindF16) ? 2 : 1;
   const int kb_elems = 128 / eb;
   p.num_kb = static_cast<int>((p.K + kb_elems - 1) / kb_elems);
   int cfg = g_force_path;
@@ -760,11 +779,13 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
   if (cfg == 1) cfg = wide ? 3 : 4;
   cudaError_t e = kind == kKindI8     ? dispatch<kKindI8>(cfg, a, lda, b, ldb, p, max_ctas, stream)
                   : kind == kKindE4M3 ? dispatch<kKindE4M3>(cfg, a, lda, b, ldb, p, max_ctas, stream)
+                  : kind == kKindF16  ? dispatch<kKindF16>(cfg, a, lda, b, ldb, p, max_ctas, stream)
                                       : dispatch<kKindBF16>(cfg, a, lda, b, ldb, p, max_ctas, stream);
   if (e == cudaErrorNotSupported && cfg >= 5 && g_force_path == 0) {
     cfg = wide ? 3 : 4;  // cluster launch unavailable: single-CTA tiles
     e = kind == kKindI8     ? dispatch<kKindI8>(cfg, a, lda, b, ldb, p, max_ctas, stream)
         : kind == kKindE4M3 ? dispatch<kKindE4M3>(cfg, a, lda, b, ldb, p, max_ctas, stream)
+        : kind == kKindF16  ? dispatch<kKindF16>(cfg, a, lda, b, ldb, p, max_ctas, stream)
                             : dispatch<kKindBF16>(cfg, a, lda, b, ldb, p, max_ctas, stream);
   }
   return e;

@@ -18,7 +18,7 @@ LIB_PATH = Path(os.environ.get("RDNA2_B200_LIBRARY",
                                Path(__file__).with_name("lib") / "librdna2_b200.so"))
 
 F32, F16, BF16, I32 = 0, 1, 2, 3
-KIND_I8, KIND_E4M3, KIND_BF16 = 0, 1, 2
+KIND_I8, KIND_E4M3, KIND_BF16, KIND_F16 = 0, 1, 2, 3
 EPI_SEPARATE, EPI_FMA, EPI_KITCHEN, EPI_NONE = 0, 1, 2, 3
 
 DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.int32: I32}
@@ -40,6 +40,12 @@ SIGNATURES = {
     "b2_quant_linear_workspace_bytes": ([_i64, _i64], _size),
     "b2_quant_linear": ([_int, _p, _int, _i64, _i64, _i64, _int, _p, _i64, _i64, _p, _i64, _p,
                          _int, _int, _p, _int, _i64, _p, _size, _p], _int),
+    "b2_w4a16_workspace_bytes": ([_i64, _i64, _i64], _size),
+    "b2_w4a16_gemm": ([_p, _int, _i64, _p, _i64, _p, _p, _i64, _int, _i64, _i64, _i64, _p, _int, _p,
+                       _i64, _p, _size, _p], _int),
+    "b2_int4_flip_nibbles": ([_p, _p, _i64, _p], _int),
+    "b2_pack_int4": ([_p, _int, _i64, _i64, _i64, _int, _int, _int, _int, _p, _p, _p, _p, _p], _int),
+    "b2_unpack_int4": ([_p, _int, _int, _p, _p, _i64, _i64, _int, _int, _p, _p], _int),
     "b2_quant_linear_noalloc_max_bytes": ([], _size),
     "b2_quant_linear_noalloc": ([_int, _p, _int, _i64, _i64, _i64, _int, _p, _i64, _i64, _p, _i64,
                                  _p, _int, _int, _p, _int, _i64, _p], _int),

@@ -1,0 +1,280 @@
+"""Group-quantized INT4 weight GEMM on sm_100a (drop-in for the reference's
+rdna2_ops/int4_weight_gemm_v07.py).
+
+Storage contract kept from the reference (int4_weight_gemm_v07.py:1-46):
+linear INT4, W = (q - zero) * scale per output row and K group, caller-owned
+packs, no hidden cache.  `PackedInt4` keeps the reference's fields and
+encodings (signed nibbles q, fp32 scales, int32 zeros = zu - 8, int32 sums,
+layouts "nk"/"kn", nibble orders "low"/"high").
+
+The B200 kernel (csrc/w4a16.cu) reads the north-star format instead --
+unsigned nibbles u = q + 8, 16-bit scales and zero points zu in the
+activation dtype -- held in a caller-owned `W4A16Weight` that
+`prepare_w4a16` builds from a PackedInt4 (the nibble flip is lossless; the
+scale cast to 16 bits is the one rounding, exactly as the north star states).
+`int4_linear_a16` accepts either; a PackedInt4 is converted per call.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as nat
+from .qlinear import qgemm_raw
+
+_GROUPS = (32, 64, 128)
+
+
+@dataclass
+class PackedInt4:
+    data: torch.Tensor
+    scales: torch.Tensor
+    zeros: torch.Tensor
+    sums: torch.Tensor
+    n: int
+    k: int
+    group_size: int
+    symmetric: bool
+    layout: str = "nk"
+    order: str = "low"
+
+    def to(self, device):
+        return PackedInt4(*(t.to(device) for t in (self.data, self.scales, self.zeros, self.sums)),
+                          self.n, self.k, self.group_size, self.symmetric, self.layout, self.order)
+
+    @property
+    def bytes(self):
+        return sum(t.numel() * t.element_size() for t in (self.data, self.scales, self.zeros, self.sums))
+
+    @property
+    def logical_stride(self):
+        return self.data.stride() if self.layout == "nk" else self.data.T.stride()
+
+
+@dataclass
+class W4A16Weight:
+    """B200 weight format: words [N, K/8] int32 of unsigned nibbles (element k
+    at bits 4*(k%8)), scales and zero points [N, K/group] in `dtype`."""
+    words: torch.Tensor
+    scales: torch.Tensor
+    zeros: torch.Tensor
+    n: int
+    k: int
+    group_size: int
+    dtype: torch.dtype
+
+    @property
+    def bytes(self):
+        return sum(t.numel() * t.element_size() for t in (self.words, self.scales, self.zeros))
+
+
+# ------------------------------------------------------------ CPU packer
+def pack_int4_cpu(w, *, group_size=64, symmetric=True, layout="nk", order="low"):
+    """Independent CPU packer (reference int4_weight_gemm_v07.py:49-82):
+    ties-to-even rounding, explicit ranges, zero groups -> scale 1, q = z = 0."""
+    if w.device.type != "cpu" or w.ndim != 2 or not w.is_floating_point():
+        raise ValueError("CPU floating-point [N,K] weight required")
+    n, k = w.shape
+    if group_size not in _GROUPS or k % group_size or layout not in ("nk", "kn") or order not in ("low", "high"):
+        raise ValueError("K must be divisible by group size 32/64/128; valid layout/order required")
+    if not torch.isfinite(w).all():
+        raise ValueError("Finite weight required")
+    x = w.float().reshape(n, k // group_size, group_size)
+    if symmetric:
+        scales = x.abs().amax(-1) / 7
+        scales = torch.where(scales == 0, torch.ones_like(scales), scales)
+        zeros = torch.zeros_like(scales, dtype=torch.int32)
+        q = torch.round(x / scales[..., None]).clamp(-7, 7).to(torch.int32)
+    else:
+        lo = torch.clamp(x.amin(-1), max=0.0)
+        hi = torch.clamp(x.amax(-1), min=0.0)
+        scales = (hi - lo) / 15
+        empty = scales == 0
+        scales = torch.where(empty, torch.ones_like(scales), scales)
+        zu = torch.round(-lo / scales).clamp(0, 15).to(torch.int32)
+        zeros = torch.where(empty, torch.zeros_like(zu), zu - 8)
+        q = (torch.round(x / scales[..., None]) + zu[..., None]).clamp(0, 15).to(torch.int32) - 8
+        q = torch.where(empty[..., None], torch.zeros_like(q), q)
+    sums = q.sum(-1, dtype=torch.int32)
+    nib = q.reshape(n, k // 8, 8).to(torch.int64) & 15
+    shifts = torch.arange(8, dtype=torch.int64) * 4
+    if order == "high":
+        shifts = 28 - shifts
+    words = (nib << shifts).sum(-1).to(torch.int32)
+    if layout == "kn":
+        words = words.T.contiguous()
+    return PackedInt4(words, scales.contiguous(), zeros.contiguous(), sums.contiguous(), n, k,
+                      group_size, bool(symmetric), layout, order)
+
+
+def unpack_int4_cpu(p, *, floating=True):
+    """CPU decode (reference int4_weight_gemm_v07.py:85-92): q - z, or (q - z) * s."""
+    words = p.data.cpu() if p.layout == "nk" else p.data.cpu().T
+    shifts = torch.arange(8, dtype=torch.int64) * 4
+    if p.order == "high":
+        shifts = 28 - shifts
+    q = ((words.to(torch.int64)[..., None] >> shifts) & 15).to(torch.int32)
+    q = torch.where(q >= 8, q - 16, q).reshape(p.n, p.k // p.group_size, p.group_size)
+    centered = q - p.zeros.cpu()[..., None]
+    if not floating:
+        return centered.reshape(p.n, p.k)
+    return (centered.float() * p.scales.cpu()[..., None]).reshape(p.n, p.k)
+
+
+# --------------------------------------------------------- GPU pack/unpack
+def _validate(p):
+    if not isinstance(p, PackedInt4) or p.data.device.type != "cuda":
+        raise ValueError("PackedInt4 on a CUDA device required")
+    nat.require_device(p.data)
+    if (p.group_size not in _GROUPS or min(p.n, p.k) <= 0 or p.k % p.group_size or p.n * p.k >= 2**31
+            or p.layout not in ("nk", "kn") or p.order not in ("low", "high")
+            or p.data.dtype != torch.int32 or not p.data.is_contiguous()
+            or tuple(p.data.shape) != ((p.n, p.k // 8) if p.layout == "nk" else (p.k // 8, p.n))):
+        raise ValueError("Invalid packed shape/storage")
+    for t, dtype in ((p.scales, torch.float32), (p.zeros, torch.int32), (p.sums, torch.int32)):
+        if (t.device != p.data.device or t.dtype != dtype or tuple(t.shape) != (p.n, p.k // p.group_size)
+                or not t.is_contiguous()):
+            raise ValueError("Invalid scale/zero/sum storage")
+    nat.eager_only(p.data, p.scales)
+
+
+def pack_int4(w, *, group_size=64, symmetric=True, layout="nk", order="low"):
+    """Device packer with pack_int4_cpu's exact semantics (csrc/w4a16.cu)."""
+    if w.ndim != 2 or not w.is_floating_point() or w.dtype not in nat.DTYPE_CODE:
+        raise ValueError("Floating [N,K] weight required")
+    dev = nat.require_device(w)
+    nat.eager_only(w)
+    n, k = w.shape
+    if group_size not in _GROUPS or k % group_size or min(n, k) <= 0 or n * k >= 2**31:
+        raise ValueError("Nonempty bounded shape and K divisible by 32/64/128 required")
+    if layout not in ("nk", "kn") or order not in ("low", "high"):
+        raise ValueError("Unknown packing layout/order")
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    data = torch.empty((n, k // 8) if layout == "nk" else (k // 8, n), device=dev, dtype=torch.int32)
+    scales = torch.empty((n, k // group_size), device=dev, dtype=torch.float32)
+    zeros = torch.empty_like(scales, dtype=torch.int32)
+    sums = torch.empty_like(zeros)
+    nat.check(nat.library().b2_pack_int4(
+        w.data_ptr(), nat.DTYPE_CODE[w.dtype], w.stride(0) if n > 1 else k, n, k, group_size,
+        int(bool(symmetric)), int(layout == "kn"), int(order == "high"), data.data_ptr(),
+        scales.data_ptr(), zeros.data_ptr(), sums.data_ptr(), nat.stream_ptr(dev)), "b2_pack_int4")
+    return PackedInt4(data, scales, zeros, sums, n, k, group_size, bool(symmetric), layout, order)
+
+
+def unpack_int4(p, *, dtype=torch.float16):
+    """Device decode: (q - z) * s as fp16/fp32, or the integer q - z as int8."""
+    _validate(p)
+    if dtype not in (torch.float16, torch.float32, torch.int8):
+        raise TypeError(dtype)
+    out = torch.empty((p.n, p.k), device=p.data.device, dtype=dtype)
+    code = {torch.float32: nat.F32, torch.float16: nat.F16, torch.int8: 3}[dtype]
+    nat.check(nat.library().b2_unpack_int4(
+        p.data.data_ptr(), int(p.layout == "kn"), int(p.order == "high"), p.scales.data_ptr(),
+        p.zeros.data_ptr(), p.n, p.k, p.group_size, code, out.data_ptr(),
+        nat.stream_ptr(p.data.device)), "b2_unpack_int4")
+    return out
+
+
+def prepare_w4a16(p, dtype=torch.bfloat16):
+    """Caller-owned B200 weight: unsigned nibbles, 16-bit scales/zero points."""
+    _validate(p)
+    if dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("W4A16 weights pair with fp16 or bf16 activations")
+    words = p.data if p.layout == "nk" else p.data.T.contiguous()
+    if p.order == "high":  # reverse the nibble order inside each word
+        w64 = words.to(torch.int64) & 0xFFFFFFFF
+        rev = torch.zeros_like(w64)
+        for j in range(8):
+            rev |= ((w64 >> (4 * j)) & 15) << (28 - 4 * j)
+        words = rev.to(torch.int32)
+    words = words.contiguous()
+    flipped = torch.empty_like(words)
+    nat.check(nat.library().b2_int4_flip_nibbles(words.data_ptr(), flipped.data_ptr(), words.numel(),
+                                                 nat.stream_ptr(words.device)), "b2_int4_flip_nibbles")
+    zu = (p.zeros + 8).to(dtype)            # integers 0..15, exact in 16 bits
+    return W4A16Weight(flipped, p.scales.to(dtype).contiguous(), zu.contiguous(), p.n, p.k,
+                       p.group_size, dtype)
+
+
+def quantize_w4a16(w, *, group_size=128, dtype=torch.bfloat16):
+    """Affine uint4 group quantization (zero point per group) straight to the
+    B200 format: pack_int4(symmetric=False) then prepare_w4a16."""
+    return prepare_w4a16(pack_int4(w, group_size=group_size, symmetric=False), dtype)
+
+
+def w4a16_gemm(a, wt, bias=None, *, workspace=None):
+    """y = a @ dequant(wt).T (+ bias) on the tcgen05 W4A16 kernel."""
+    if not isinstance(wt, W4A16Weight):
+        raise TypeError("W4A16Weight required")
+    if a.dtype != wt.dtype or a.ndim != 2 or a.shape[1] != wt.k:
+        raise ValueError(f"Matching {wt.dtype} activation [M,{wt.k}] required")
+    dev = nat.require_device(a, wt.words, bias)
+    if a.stride(1) != 1 or (a.shape[0] > 1 and (a.stride(0) * 2) % 16) or a.data_ptr() % 16:
+        a = a.contiguous()
+    m = a.shape[0]
+    out = torch.empty((m, wt.n), device=dev, dtype=a.dtype)
+    lib = nat.library()
+    need = lib.b2_w4a16_workspace_bytes(m, wt.n, wt.k)
+    if need and (workspace is None or workspace.numel() < need):
+        workspace = torch.empty(need, device=dev, dtype=torch.uint8)
+    nat.check(lib.b2_w4a16_gemm(
+        a.data_ptr(), nat.DTYPE_CODE[a.dtype], a.stride(0) if m > 1 else wt.k, wt.words.data_ptr(),
+        wt.k // 8, wt.scales.data_ptr(), wt.zeros.data_ptr(), wt.k // wt.group_size, wt.group_size,
+        m, wt.n, wt.k, nat.ptr(bias), nat.DTYPE_CODE[bias.dtype] if bias is not None else 0,
+        out.data_ptr(), wt.n, None if not need else workspace.data_ptr(), need, nat.stream_ptr(dev)),
+        "b2_w4a16_gemm")
+    return out
+
+
+def int4_linear_a16(a, p, *, bias=None, method="dequant", prepared=None, tile=(64, 64, 32),
+                    num_warps=4, return_kernel=False):
+    """16-bit activation x INT4 weight (reference int4_weight_gemm_v07.py:540-564).
+
+    Methods "dequant" and "dot2" run the fused tcgen05 kernel (the dequantized
+    weight never leaves shared memory); "prepared" uses a caller-owned
+    `W4A16Weight`.  fp16 activations give fp16 output, bf16 give bf16.
+    """
+    if method not in ("dequant", "dot2", "prepared"):
+        raise ValueError(method)
+    if method == "prepared":
+        if not isinstance(prepared, W4A16Weight):
+            raise ValueError("W4A16Weight prepared weight required")
+        wt = prepared
+    else:
+        _validate(p)
+        wt = None
+    if a.dtype not in (torch.float16, torch.bfloat16) or a.ndim != 2:
+        raise ValueError("Matching FP16/BF16 activation [M,K] required")
+    k = wt.k if wt is not None else p.k
+    n = wt.n if wt is not None else p.n
+    if a.shape[1] != k or min(a.stride()) <= 0 or a.shape[0] * n >= 2**31:
+        raise ValueError("Unsupported shape/stride")
+    if bias is not None and (bias.dtype != a.dtype or bias.shape != (n,) or bias.device != a.device):
+        raise ValueError("Bias [N] of the activation dtype required")
+    nat.eager_only(a, bias)
+    if method == "dot2" and (len(tile) != 3 or any(x not in (16, 32, 64, 128) for x in tile) or k % tile[2]):
+        raise ValueError("Supported dot2 tile required")
+    if wt is None:
+        wt = prepare_w4a16(p, a.dtype)
+    if wt.dtype != a.dtype:
+        raise ValueError("Prepared weight dtype must match the activation dtype")
+    out = w4a16_gemm(a, wt, bias)
+    kernel = {"name": "w4a16_kernel (tcgen05 kind::f16, swap-AB)", "arch": "sm_100a"}
+    return (out, kernel) if return_kernel else out
+
+
+def dense_linear(a, w, bias=None):
+    """16-bit dense GEMM on the tcgen05 kernel (kind::f16): a [M,K] @ w[N,K].T."""
+    if a.dtype != w.dtype or a.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("fp16/bf16 operands of one dtype required")
+    dev = nat.require_device(a, w, bias)
+    m, k = a.shape
+    n = w.shape[0]
+    ones_m = torch.ones(m, device=dev, dtype=torch.float32)
+    ones_n = torch.ones(1, device=dev, dtype=torch.float32)
+    out = torch.empty((m, n), device=dev, dtype=a.dtype)
+    kind = nat.KIND_BF16 if a.dtype == torch.bfloat16 else nat.KIND_F16
+    return qgemm_raw(kind, a.view(torch.int16), w.view(torch.int16), ones_m, ones_n, bias,
+                     nat.EPI_SEPARATE, out)

@@ -125,7 +125,7 @@ def qgemm_raw(kind, a, w, a_scale, w_scale, bias, epilogue, out):
     layouts the TMA cannot read are repacked to K-major first)."""
     m, k = a.shape
     n = w.shape[0]
-    eb = 2 if kind == nat.KIND_BF16 else 1
+    eb = 2 if kind in (nat.KIND_BF16, nat.KIND_F16) else 1
     dev = out.device
     if m == 0 or n == 0:
         return out

@@ -1,0 +1,128 @@
+"""INT4 path on the GPU: device packer/decoder bit-exact against the
+reference's pack_int4_cpu golden vectors, and the tcgen05 W4A16 GEMM against
+the fp64 CPU oracle at every BASELINE config-3 token count.
+
+W4A16 tolerance: the dequantized 16-bit weights are bit-exact by
+construction; the GEMM accumulates exact fp32 products in an order the
+tensor core chooses, so outputs must lie within 1 ulp of the 16-bit output
+type at |ref| plus 2^-12 of the sum of |a*w| products (fp32 accumulation)."""
+import numpy as np
+import pytest
+
+import oracle
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from rdna2_ops import _native as nat  # noqa: E402
+from rdna2_ops import int4_weight_gemm_v07 as i4  # noqa: E402
+
+ODT = {torch.float16: oracle.F16, torch.bfloat16: oracle.BF16}
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _status():
+    nat.device_status(reset=True)
+    yield
+    assert nat.device_status() == 0
+
+
+@pytest.mark.parametrize("g", [32, 64, 128])
+@pytest.mark.parametrize("sym", [True, False])
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+@pytest.mark.parametrize("order", ["low", "high"])
+def test_pack_int4_matches_reference_golden(golden, g, sym, layout, order):
+    """Device packer == reference pack_int4_cpu on bench_int4_v07.py:85-95's
+    smoke weights (zero row, full nibble ranges) for every combination."""
+    z = golden("int4_packing.npz")
+    key = f"g{g}_{'sym' if sym else 'aff'}_{layout}_{order}"
+    w = torch.from_numpy(z["w"]).cuda()
+    p = i4.pack_int4(w, group_size=g, symmetric=sym, layout=layout, order=order)
+    for f in ("data", "scales", "zeros", "sums"):
+        got = getattr(p, f).cpu().numpy()
+        ref = z[key + "_" + f]
+        assert got.dtype == ref.dtype and np.array_equal(got.view(np.uint32), ref.view(np.uint32)), f
+    assert np.array_equal(i4.unpack_int4(p, dtype=torch.int8).cpu().numpy().astype(np.int32),
+                          z[key + "_centered"])
+    assert np.array_equal(i4.unpack_int4(p, dtype=torch.float32).cpu().numpy().view(np.uint32),
+                          z[key + "_float"].view(np.uint32))
+
+
+def _ref_w4a16(a_bits, a_code, p_cpu, dtype):
+    """fp64 oracle: bf16/fp16-rounded scales, w = round((u - zu) * s), fp64 dot."""
+    s16 = p_cpu.scales.to(dtype).float().numpy()
+    w = oracle.dequant_int4(p_cpu.data.numpy(), s16, p_cpu.zeros.float().numpy(), p_cpu.group_size,
+                            out_dtype=ODT[dtype])
+    a = oracle.decode(a_bits, a_code)
+    return oracle.gemm_f32_f64(a, w), oracle.gemm_f32_f64(np.abs(a), np.abs(w))
+
+
+def _bits(t):
+    return t.detach().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def _check(y, ref, absref, dtype, bias=None):
+    got = oracle.decode(_bits(y), ODT[dtype]).astype(np.float64)
+    if bias is not None:
+        ref = ref + oracle.decode(_bits(bias), ODT[dtype]).astype(np.float64)[None, :]
+    ulp = np.maximum(np.abs(ref), 2.0 ** -14) * (2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11)
+    tol = ulp + 2.0 ** -12 * absref
+    bad = np.abs(got - ref) > tol
+    assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance"
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m,n,k,g", [(17, 19, 384, 32), (17, 19, 384, 64), (17, 19, 384, 128),
+                                     (33, 300, 1024, 128), (200, 520, 512, 64)])
+def test_w4a16_small_shapes(dtype, m, n, k, g):
+    gen = torch.Generator().manual_seed(20261107 + m + n)
+    w = torch.randn((n, k), generator=gen) * 0.2
+    w[0] = 0
+    p_cpu = i4.pack_int4_cpu(w, group_size=g, symmetric=False)
+    a = (torch.randn((m, k), generator=gen) * 0.5).to(dtype)
+    bias = (torch.randn(n, generator=gen) * 0.1).to(dtype)
+    y = i4.int4_linear_a16(a.cuda(), p_cpu.to("cuda"), bias=bias.cuda())
+    ref, absref = _ref_w4a16(_bits(a), ODT[dtype], p_cpu, dtype)
+    _check(y, ref, absref, dtype, bias)
+
+
+@pytest.mark.parametrize("m", [1, 16, 128, 2048])
+def test_w4a16_config3(m):
+    """bf16 A [M,4096], W [14336,4096] N(0,0.02) affine uint4
+    g128 with bf16 scales/zeros, bf16 out; oracle on a row/column sample."""
+    dtype = torch.bfloat16
+    n, k = 14336, 4096
+    gen = torch.Generator(device="cuda").manual_seed(20261107)
+    w = torch.randn((n, k), generator=gen, device="cuda") * 0.02
+    wt = i4.quantize_w4a16(w, group_size=128, dtype=dtype)
+    a = torch.randn((m, k), generator=gen, device="cuda").to(dtype)
+    y = i4.w4a16_gemm(a, wt)
+    rng = np.random.default_rng(m)
+    rows = np.arange(m) if m <= 64 else np.sort(rng.choice(m, 64, replace=False))
+    cols = np.sort(rng.choice(n, 384, replace=False))
+    p = i4.pack_int4(w[torch.from_numpy(cols).cuda()], group_size=128, symmetric=False)
+    p_cpu = p.to("cpu")
+    ref, absref = _ref_w4a16(_bits(a[torch.from_numpy(rows).cuda()]), ODT[dtype], p_cpu, dtype)
+    _check(y[torch.from_numpy(rows).cuda()][:, torch.from_numpy(cols).cuda()], ref, absref, dtype)
+
+
+def test_w4a16_deterministic_split_k():
+    dtype = torch.bfloat16
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    w = torch.randn((4096, 4096), generator=gen, device="cuda") * 0.02
+    wt = i4.quantize_w4a16(w, group_size=128, dtype=dtype)
+    a = torch.randn((8, 4096), generator=gen, device="cuda").to(dtype)
+    assert nat.library().b2_w4a16_workspace_bytes(8, 4096, 4096) > 0  # split-K engaged
+    y1, y2 = i4.w4a16_gemm(a, wt), i4.w4a16_gemm(a, wt)
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_dense_linear_kind_f16(dtype):
+    gen = torch.Generator().manual_seed(8)
+    m, n, k = 300, 520, 1024
+    a = torch.randn((m, k), generator=gen).to(dtype)
+    w = (torch.randn((n, k), generator=gen) * 0.05).to(dtype)
+    y = i4.dense_linear(a.cuda(), w.cuda())
+    af, wf = oracle.decode(_bits(a), ODT[dtype]), oracle.decode(_bits(w), ODT[dtype])
+    _check(y, oracle.gemm_f32_f64(af, wf), oracle.gemm_f32_f64(np.abs(af), np.abs(wf)), dtype)

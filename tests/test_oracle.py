@@ -159,3 +159,21 @@ def test_int4_packer_baseline_format(golden):
     p = oracle.pack_int4(z["big_w"], 128, False, "low")
     for f in ("data", "scales", "zeros", "sums"):
         assert np.array_equal(p[f], z["big_" + f])
+
+
+@pytest.mark.parametrize("g", [32, 64, 128])
+@pytest.mark.parametrize("sym", [True, False])
+def test_package_pack_int4_cpu_matches_golden(golden, g, sym):
+    """The package's CPU packer (part of the reference API surface) equals the
+    reference's pack_int4_cpu output on the smoke weights."""
+    torch = pytest.importorskip("torch")
+    from rdna2_ops.int4_weight_gemm_v07 import pack_int4_cpu, unpack_int4_cpu
+    z = golden("int4_packing.npz")
+    for layout in ("nk", "kn"):
+        for order in ("low", "high"):
+            key = f"g{g}_{'sym' if sym else 'aff'}_{layout}_{order}"
+            p = pack_int4_cpu(torch.from_numpy(z["w"]), group_size=g, symmetric=sym, layout=layout,
+                              order=order)
+            for f in ("data", "scales", "zeros", "sums"):
+                assert np.array_equal(getattr(p, f).numpy(), z[key + "_" + f]), (key, f)
+            assert np.array_equal(unpack_int4_cpu(p, floating=False).numpy(), z[key + "_centered"])
