@@ -11,7 +11,8 @@
  *     (except b2_device_status, which is documented as synchronous);
  *   - all device pointers belong to the current CUDA device.
  *
- * dtype codes:  0 = float32, 1 = float16, 2 = bfloat16, 3 = int32
+ * dtype codes:  0 = float32, 1 = float16, 2 = bfloat16, 3 = int32,
+ *               4 = float8 e4m3fn, 5 = float8 e5m2 (activation-prologue inputs)
  * epilogue:     0 = separate  v = float(acc)*(sa*sb) [+ bias] in fp32, then cast
  *                               (rdna2_ops/int8_gemm.py:53-63, rounding="separate")
  *               1 = fma       v = fma(float(acc), sa*sb, bias)  (rounding="fused")
@@ -64,10 +65,13 @@ int b2_device_status(int* status, int reset);
 
 /* Activation prologue: optional block-Hadamard rotation, per-row absmax,
  * round-to-nearest-even quantization.
- *   x      [M,K] of x_dtype (0/1/2), row stride ldx elements
+ *   x      [M,K] of x_dtype (0/1/2, or fp8 4/5), row stride ldx elements
  *   block  0 or 1 = no rotation; else a power of two dividing K (<= 4096)
- *   quant  0 = int8 (scale = absmax/127, codes in [-127,127]);
- *          1 = e4m3 (scale = absmax/448, saturating)
+ *   quant  0 = int8 (scale = absmax/127, round half even, codes in [-127,127]);
+ *          1 = e4m3 (scale = absmax/448, saturating);
+ *          2 = int8 with the reference row quantizer's rounding
+ *              (rdna2_ops/fp8_weight_gemm_v06.py:87-90: step = max(absmax/127,
+ *              1e-20), floor(z + 0.5) / ceil(z - 0.5) in fp32)
  *   q      [M,K] 1-byte codes, row stride ldq bytes (columns >= K untouched)
  *   scale  [M] fp32
  * Replaces Kitchen's _rotate_activation + quantize_int8_rowwise at
@@ -132,6 +136,12 @@ int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* wq, int64
                   const void* scales, const void* zeros, int64_t ldsz, int group, int64_t M,
                   int64_t N, int64_t K, const void* bias, int bias_dtype, void* out, int64_t ldo,
                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Exact fp8 decode (rdna2_ops/fp8_weight_gemm_v06.py:22-46, 109-124):
+ * w [rows, cols] of fp8_dtype (4 e4m3fn, 5 e5m2), row stride ld bytes ->
+ * out of out_dtype (0 fp32, 1 fp16), row stride ldo elements. */
+int b2_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld, int out_dtype,
+                  void* out, int64_t ldo, void* stream);
 
 /* dst = src ^ 0x88888888 over n_words words: converts the reference's signed
  * nibbles (q = u - 8, PackedInt4 at int4_weight_gemm_v07.py:20-46) to the

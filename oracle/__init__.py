@@ -40,6 +40,8 @@ def lib():
         "b2o_rotate_rows": [_p, _int, _i64, _i64, _i64, _int, _p],
         "b2o_quant_rows_int8": [_p, _i64, _i64, _p, _i64, _p],
         "b2o_quant_rows_e4m3": [_p, _i64, _i64, _p, _i64, _p],
+        "b2o_quant_rows_ref": [_p, _i64, _i64, _p, _i64, _p],
+        "b2o_decode_e5m2": [_p, _i64, _p],
         "b2o_gemm_s8": [_p, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _int],
         "b2o_epilogue_s32": [_p, _i64, _p, _p, _i64, _p, _int, _i64, _i64, _int, _p, _int, _i64],
         "b2o_epilogue_f32": [_p, _i64, _p, _p, _p, _int, _i64, _i64, _p, _int, _i64],
@@ -136,6 +138,23 @@ def quant_rows_e4m3(xf):
     s = np.empty(m, np.float32)
     lib().b2o_quant_rows_e4m3(_ptr(xf), m, k, _ptr(q), k, _ptr(s))
     return q, s
+
+
+def quant_rows_ref(xf):
+    """The reference's _quant_rows (fp8_weight_gemm_v06.py:76-92)."""
+    xf = _c(xf, np.float32)
+    m, k = xf.shape
+    q = np.empty((m, k), np.int8)
+    s = np.empty(m, np.float32)
+    lib().b2o_quant_rows_ref(_ptr(xf), m, k, _ptr(q), k, _ptr(s))
+    return q, s
+
+
+def decode_e5m2(codes):
+    codes = _c(codes, np.uint8)
+    out = np.empty(codes.shape, np.float32)
+    lib().b2o_decode_e5m2(_ptr(codes), codes.size, _ptr(out))
+    return out
 
 
 def act_quant_int8(x, dtype, block):

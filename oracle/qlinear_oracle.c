@@ -188,6 +188,36 @@ void b2o_quant_rows_int8(const float* x, int64_t M, int64_t K, int8_t* q,
   }
 }
 
+/* The reference's in-repo row quantizer _quant_rows
+ * (rdna2-ops/rdna2_ops/fp8_weight_gemm_v06.py:76-92): step = max(absmax/127,
+ * 1e-20); z = x/step; q = z >= 0 ? floor(z + 0.5) : ceil(z - 0.5) with the
+ * fp32 rounding of z +- 0.5; clamp to [-127, 127]. */
+void b2o_quant_rows_ref(const float* x, int64_t M, int64_t K, int8_t* q, int64_t ldq,
+                        float* scale) {
+#pragma omp parallel for schedule(static)
+  for (int64_t r = 0; r < M; r++) {
+    const float* v = x + r * K;
+    float amax = 0.0f;
+    for (int64_t k = 0; k < K; k++) { float a = fabsf(v[k]); if (a > amax) amax = a; }
+    float s = amax / 127.0f;
+    if (s < 1.0e-20f) s = 1.0e-20f;
+    for (int64_t k = 0; k < K; k++) {
+      float z = v[k] / s;
+      float t = z >= 0.0f ? floorf(z + 0.5f) : ceilf(z - 0.5f);
+      if (t > 127.0f) t = 127.0f;
+      if (t < -127.0f) t = -127.0f;
+      q[r * ldq + k] = (int8_t)t;
+    }
+    scale[r] = s;
+  }
+}
+
+float b2o_e5m2_to_f32(uint8_t b) { return b2o_f16_to_f32((uint16_t)((uint16_t)b << 8)); }
+
+void b2o_decode_e5m2(const uint8_t* x, int64_t n, float* out) {
+  for (int64_t i = 0; i < n; i++) out[i] = b2o_e5m2_to_f32(x[i]);
+}
+
 /* Per-row e4m3: s = absmax/448, s := 1 when not positive, q = e4m3_rn_sat(x/s). */
 void b2o_quant_rows_e4m3(const float* x, int64_t M, int64_t K, uint8_t* q,
                          int64_t ldq, float* scale) {

@@ -26,6 +26,18 @@ struct Raw8 {
 
 template <int DT>
 __device__ __forceinline__ void load_raw(const void* x, int64_t off, bool vec, int valid, Raw8& r) {
+  if constexpr (DT == kE4M3 || DT == kE5M2) {
+    uint32_t lo = 0, hi = 0;
+    const uint8_t* b = static_cast<const uint8_t*>(x) + off;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t v = j < valid ? b[j] : 0u;
+      if (j < 4) lo |= v << (8 * j);
+      else hi |= v << (8 * (j - 4));
+    }
+    r.a = make_uint4(lo, hi, 0u, 0u);
+    return;
+  }
   if (vec && valid == 8) {
     if constexpr (DT == kF32) {
       const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(x) + off);
@@ -60,7 +72,11 @@ __device__ __forceinline__ void load_raw(const void* x, int64_t off, bool vec, i
 
 template <int DT>
 __device__ __forceinline__ void unpack_raw(const Raw8& r, float (&v)[8]) {
-  if constexpr (DT == kF32) {
+  if constexpr (DT == kE4M3 || DT == kE5M2) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = fp8_to_float(static_cast<uint8_t>(((j < 4 ? r.a.x : r.a.y) >> (8 * (j & 3))) & 0xffu), DT);
+  } else if constexpr (DT == kF32) {
     v[0] = __uint_as_float(r.a.x); v[1] = __uint_as_float(r.a.y);
     v[2] = __uint_as_float(r.a.z); v[3] = __uint_as_float(r.a.w);
     v[4] = __uint_as_float(r.b.x); v[5] = __uint_as_float(r.b.y);
@@ -116,12 +132,25 @@ __device__ __forceinline__ uint32_t quant_e4m3(float v, float s, float r, bool f
   return static_cast<uint32_t>(__nv_cvt_float_to_fp8(__fdiv_rn(v, s), __NV_SATFINITE, __NV_E4M3));
 }
 
+// The reference's in-repo row quantizer _quant_rows
+// (rdna2_ops/fp8_weight_gemm_v06.py:87-90): z = x / step, then
+// floor(z + 0.5) or ceil(z - 0.5) in fp32 (half away from zero, including the
+// fp32 rounding of z +- 0.5), clamped to [-127, 127].
+__device__ __forceinline__ uint32_t quant_rows_ref(float v, float s) {
+  const float z = __fdiv_rn(v, s);
+  float q = z >= 0.0f ? floorf(__fadd_rn(z, 0.5f)) : ceilf(__fsub_rn(z, 0.5f));
+  q = fminf(fmaxf(q, -127.0f), 127.0f);
+  return static_cast<uint32_t>(static_cast<int>(q)) & 0xffu;
+}
+
 template <int QUANT>
 __device__ __forceinline__ uint32_t pack4(const float* v, float s, float r, bool fast) {
   uint32_t c[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
-    c[i] = QUANT == 0 ? quant_int8(v[i], s, r, fast) : quant_e4m3(v[i], s, r, fast);
+    c[i] = QUANT == 0 ? quant_int8(v[i], s, r, fast)
+         : QUANT == 1 ? quant_e4m3(v[i], s, r, fast)
+                      : quant_rows_ref(v[i], s);
   return __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
 }
 
@@ -228,8 +257,12 @@ __global__ void __launch_bounds__(128)
       for (int w = 0; w < wpr; ++w) amax = fmaxf(amax, s_max[parity][g * wpr + w]);
       parity ^= 1;
     }
-    float sc = __fdiv_rn(amax, QUANT == 0 ? 127.0f : 448.0f);
-    if (!(sc > 0.0f)) sc = 1.0f;
+    float sc = __fdiv_rn(amax, QUANT == 1 ? 448.0f : 127.0f);
+    if constexpr (QUANT == 2) {
+      sc = fmaxf(sc, 1.0e-20f);                    // step floor of _quant_rows
+    } else {
+      if (!(sc > 0.0f)) sc = 1.0f;
+    }
     if (!live) continue;
     const float rcp = __frcp_rn(sc);
     const bool fast = sc > 1e-30f && sc < 1e30f;
@@ -312,20 +345,50 @@ cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   if (M == 0) return cudaSuccess;
   int wpr = 1, spw = 1;
   if (!choose_layout(K, block, &wpr, &spw)) return cudaErrorInvalidValue;
-  const int eb = x_dtype == kF32 ? 4 : 2;
+  const int eb = x_dtype == kF32 ? 4 : (x_dtype == kE4M3 || x_dtype == kE5M2) ? 1 : 2;
   const int vin = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ldx * eb) % 16 == 0);
   const int vout = (reinterpret_cast<uintptr_t>(q) % 8 == 0) && (ldq % 8 == 0);
   const float inv = block > 1 ? static_cast<float>(1.0 / sqrt(static_cast<double>(block))) : 1.0f;
   uint8_t* qb = static_cast<uint8_t*>(q);
   const int k = static_cast<int>(K);
-  if (quant == 0) {
-    if (x_dtype == kF32) return launch_spw<kF32, 0>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
-    if (x_dtype == kF16) return launch_spw<kF16, 0>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
-    return launch_spw<kBF16, 0>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
+#define B2_AQ(DT, Q) return launch_spw<DT, Q>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout)
+#define B2_AQ_DT(Q)                 \
+  switch (x_dtype) {                \
+    case kF32: B2_AQ(kF32, Q);      \
+    case kF16: B2_AQ(kF16, Q);      \
+    case kBF16: B2_AQ(kBF16, Q);    \
+    case kE4M3: B2_AQ(kE4M3, Q);    \
+    case kE5M2: B2_AQ(kE5M2, Q);    \
+    default: return cudaErrorInvalidValue; \
   }
-  if (x_dtype == kF32) return launch_spw<kF32, 1>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
-  if (x_dtype == kF16) return launch_spw<kF16, 1>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
-  return launch_spw<kBF16, 1>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout);
+  if (quant == 0) { B2_AQ_DT(0) }
+  if (quant == 1) { B2_AQ_DT(1) }
+  B2_AQ_DT(2)
+#undef B2_AQ_DT
+#undef B2_AQ
+}
+
+// fp8 (e4m3fn / e5m2) -> fp32 / fp16 decode, exact for every finite pattern;
+// NaN and infinity classes preserved (reference _decode_bits /
+// _decode_weight, rdna2_ops/fp8_weight_gemm_v06.py:22-46).
+__global__ void fp8_decode_kernel(const uint8_t* __restrict__ w, int fp8_dtype, int64_t rows, int64_t cols,
+                                  int64_t ld, int out_dtype, void* __restrict__ out, int64_t ldo) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= rows * cols) return;
+  const int64_t r = i / cols, c = i % cols;
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(w[r * ld + c]),
+                                               fp8_dtype == kE4M3 ? __NV_E4M3 : __NV_E5M2);
+  if (out_dtype == kF16) static_cast<__half_raw*>(out)[r * ldo + c] = h;
+  else static_cast<float*>(out)[r * ldo + c] = __half2float(__half(h));
+}
+
+cudaError_t run_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld,
+                           int out_dtype, void* out, int64_t ldo, cudaStream_t stream) {
+  const int64_t total = rows * cols;
+  if (total == 0) return cudaSuccess;
+  fp8_decode_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, stream>>>(
+      static_cast<const uint8_t*>(w), fp8_dtype, rows, cols, ld, out_dtype, out, ldo);
+  return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ repack

@@ -12,7 +12,7 @@
 namespace b2 {
 
 // dtype codes shared with include/b2_qlinear.h
-enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2, kI32 = 3 };
+enum DType : int { kF32 = 0, kF16 = 1, kBF16 = 2, kI32 = 3, kE4M3 = 4, kE5M2 = 5 };
 enum Epilogue : int { kEpiSeparate = 0, kEpiFma = 1, kEpiKitchen = 2, kEpiNone = 3 };
 enum Kind : int { kKindI8 = 0, kKindE4M3 = 1, kKindBF16 = 2, kKindF16 = 3 };
 
@@ -307,10 +307,18 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 }
 
 // ------------------------------------------------------------ dtype helpers
+// Exact fp8 -> fp32 (every finite e4m3 / e5m2 value is an fp16 value).
+__device__ __forceinline__ float fp8_to_float(uint8_t b, int dtype) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b),
+                                               dtype == kE4M3 ? __NV_E4M3 : __NV_E5M2);
+  return __half2float(__half(h));
+}
+
 __device__ __forceinline__ float load_as_float(const void* p, int dtype, int64_t i) {
   if (dtype == kF32) return static_cast<const float*>(p)[i];
   if (dtype == kF16) return __half2float(static_cast<const __half*>(p)[i]);
-  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  if (dtype == kBF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+  return fp8_to_float(static_cast<const uint8_t*>(p)[i], dtype);
 }
 
 }  // namespace b2

@@ -36,10 +36,14 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
 void set_gemm_path(int path);
 int pair_capacity();
 
-// Per-row rotate + quantize (quant 0 = int8 /127, 1 = e4m3 /448).
+// Per-row rotate + quantize (quant 0 = int8 /127 RNE, 1 = e4m3 /448, 2 = the
+// reference row quantizer: int8, half away from zero, step floor 1e-20).
 cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                           int block, int quant, void* q, int64_t ldq, float* scale,
                           cudaStream_t stream);
+
+cudaError_t run_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld,
+                           int out_dtype, void* out, int64_t ldo, cudaStream_t stream);
 
 // dst[r, c] = src[r*s_row + c*s_col] for c < cols, 0 for cols <= c < ldd.
 cudaError_t run_repack(const void* src, int elem_bytes, int64_t rows, int64_t cols, int64_t s_row,

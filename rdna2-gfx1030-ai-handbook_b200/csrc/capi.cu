@@ -93,7 +93,7 @@ int b2_set_gemm_path(int path) {
 int b2_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block, int quant,
                  void* q, int64_t ldq, float* scale, void* stream) {
   if (M < 0 || K < 1 || M > INT32_MAX || K > 16384) return fail();
-  if (x_dtype < 0 || x_dtype > 2 || quant < 0 || quant > 1) return fail();
+  if (x_dtype < 0 || x_dtype > 5 || x_dtype == 3 || quant < 0 || quant > 2) return fail();
   if (!valid_block(block, K)) return fail();
   if (M == 0) return 0;
   if (!x || !q || !scale || ldx < K || ldq < K) return fail();
@@ -182,6 +182,17 @@ int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* wq, int64
                                         static_cast<const uint16_t*>(zeros), ldsz, group, M, N, K, bias,
                                         bias_dtype, out, ldo, static_cast<float*>(workspace),
                                         workspace_bytes, splits, static_cast<cudaStream_t>(stream)));
+}
+
+int b2_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld, int out_dtype,
+                  void* out, int64_t ldo, void* stream) {
+  if ((fp8_dtype != b2::kE4M3 && fp8_dtype != b2::kE5M2) || (out_dtype != b2::kF32 && out_dtype != b2::kF16))
+    return fail();
+  if (rows < 0 || cols < 0 || ld < cols || ldo < cols) return fail();
+  if (rows == 0 || cols == 0) return 0;
+  if (!w || !out) return fail();
+  return static_cast<int>(b2::run_fp8_decode(w, fp8_dtype, rows, cols, ld, out_dtype, out, ldo,
+                                             static_cast<cudaStream_t>(stream)));
 }
 
 int b2_int4_flip_nibbles(const void* src, void* dst, int64_t n_words, void* stream) {

@@ -17,11 +17,12 @@ import torch
 LIB_PATH = Path(os.environ.get("RDNA2_B200_LIBRARY",
                                Path(__file__).with_name("lib") / "librdna2_b200.so"))
 
-F32, F16, BF16, I32 = 0, 1, 2, 3
+F32, F16, BF16, I32, E4M3, E5M2 = 0, 1, 2, 3, 4, 5
 KIND_I8, KIND_E4M3, KIND_BF16, KIND_F16 = 0, 1, 2, 3
 EPI_SEPARATE, EPI_FMA, EPI_KITCHEN, EPI_NONE = 0, 1, 2, 3
 
-DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.int32: I32}
+DTYPE_CODE = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16, torch.int32: I32,
+              torch.float8_e4m3fn: E4M3, torch.float8_e5m2: E5M2}
 
 _p, _i64, _int, _size = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
 
@@ -44,6 +45,7 @@ SIGNATURES = {
     "b2_w4a16_gemm": ([_p, _int, _i64, _p, _i64, _p, _p, _i64, _int, _i64, _i64, _i64, _p, _int, _p,
                        _i64, _p, _size, _p], _int),
     "b2_int4_flip_nibbles": ([_p, _p, _i64, _p], _int),
+    "b2_fp8_decode": ([_p, _int, _i64, _i64, _i64, _int, _p, _i64, _p], _int),
     "b2_pack_int4": ([_p, _int, _i64, _i64, _i64, _int, _int, _int, _int, _p, _p, _p, _p, _p], _int),
     "b2_unpack_int4": ([_p, _int, _int, _p, _p, _i64, _i64, _int, _int, _p, _p], _int),
     "b2_quant_linear_noalloc_max_bytes": ([], _size),

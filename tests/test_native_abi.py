@@ -63,7 +63,7 @@ def test_qgemm_empty_is_noop():
 def test_act_quant_rejects_bad_arguments():
     lib = nat.library()
     ok = dict(x=16, dt=1, M=2, K=256, ldx=256, block=128, quant=0, q=16, ldq=256, s=16, st=None)
-    for bad in (dict(block=96), dict(block=512), dict(dt=3), dict(quant=2), dict(ldx=100),
+    for bad in (dict(block=96), dict(block=512), dict(dt=3), dict(dt=6), dict(quant=3), dict(ldx=100),
                 dict(K=20000), dict(x=None)):
         a = dict(ok, **bad)
         assert lib.b2_act_quant(*a.values()) == EINVAL, bad
