@@ -332,7 +332,7 @@ def run_b200(args, rank, world, local_rank):
     # ---- all-gather that reassembles the column-parallel output (reported apart)
     gather = None
     if world > 1:
-        full = torch.empty((world, M, N), device=dev, dtype=torch.float16)
+        full = torch.empty((world * M, N), device=dev, dtype=torch.float16)
         for _ in range(3):
             dist.all_gather_into_tensor(full, out)
         torch.cuda.synchronize()
