@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sets", type=int, default=4, help="input sets cycled to defeat L2 reuse")
+    ap.add_argument("--workload", default="c2",
+                    help="c2 (headline, default), c1, c3m1/c3m16/c3m128/c3m2048 (W4A16), "
+                         "c4m1/c4m2048 (FP8); non-c2 workloads run on one GPU")
     return ap.parse_args()
 
 
@@ -391,6 +394,103 @@ def run_b200(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def run_workload(args):
+    """Configs 1, 3 and 4 of the benchmark plan on one GPU: one JSON line with
+    the same timing discipline (warm-up, CUDA events on the launch stream,
+    weights cycled over enough copies to exceed L2) and a roofline for the
+    op's own kernel."""
+    import torch
+    import rdna2_ops
+    from rdna2_ops import _native as nat
+    from rdna2_ops import int4_weight_gemm_v07 as i4
+    from rdna2_ops import qlinear
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED)
+    pk = peaks()
+    name = args.workload
+    sets = max(args.sets, 8)
+    if name == "c1":
+        m, n, k = 1024, 3072, 3072
+        xs = [(torch.randn((m, k), generator=gen, device=dev)).half() for _ in range(sets)]
+        w = torch.randn((n, k), generator=gen, device=dev) * 0.02
+        wq, sw = qlinear.quantize_weight(w)
+        wqs = [wq.clone() for _ in range(sets)]
+        bias = (torch.randn(n, generator=gen, device=dev) * 0.02).half()
+        ws = torch.empty(nat.library().b2_quant_linear_workspace_bytes(m, k), device=dev, dtype=torch.uint8)
+        step = lambda i: rdna2_ops.w8a8_linear(xs[i % sets], wqs[i % sets], sw, bias,
+                                               out_dtype=torch.float16, workspace=ws)
+        metric, flops, launches = "W8A8 INT8 linear TOPS (config 1)", 2.0 * m * n * k, 2
+        bound, peak, unit, traffic = "tensor", 2.0 * pk["bf16_tflops"], "TOPS", None
+        dtype = "int8"
+    elif name.startswith("c3m"):
+        m, n, k = int(name[3:]), 14336, 4096
+        w = torch.randn((n, k), generator=gen, device=dev) * 0.02
+        wt = i4.quantize_w4a16(w, group_size=128, dtype=torch.bfloat16)
+        del w
+        wts = [wt] + [i4.W4A16Weight(wt.words.clone(), wt.scales.clone(), wt.zeros.clone(), n, k, 128,
+                                     torch.bfloat16) for _ in range(sets - 1)]
+        xs = [torch.randn((m, k), generator=gen, device=dev).to(torch.bfloat16) for _ in range(sets)]
+        need = nat.library().b2_w4a16_workspace_bytes(m, n, k, 128)
+        ws = torch.empty(max(need, 1), device=dev, dtype=torch.uint8)
+        step = lambda i: i4.w4a16_gemm(xs[i % sets], wts[i % sets], workspace=ws)
+        metric, flops = f"W4A16 GEMM TFLOPS (config 3, M={m})", 2.0 * m * n * k
+        launches = 2 if need else 1
+        traffic = n * k // 2 + 2 * n * (k // 128) * 2 + m * k * 2 + m * n * 2
+        if m <= 128:
+            bound, peak, unit = "hbm", pk["hbm_gbs"], "GB/s"
+        else:
+            bound, peak, unit = "tensor", pk["bf16_tflops"], "TFLOP/s"
+        dtype = "bf16"
+    elif name.startswith("c4m"):
+        m, n, k = int(name[3:]), 5120, 5120
+        w = torch.randn((n, k), generator=gen, device=dev) * 0.02
+        wq, sw = qlinear.quantize_weight(w, quant="e4m3")
+        wqs = [wq.clone() for _ in range(sets)]
+        xs = [torch.randn((m, k), generator=gen, device=dev).to(torch.bfloat16) for _ in range(sets)]
+        ws = torch.empty(nat.library().b2_quant_linear_workspace_bytes(m, k), device=dev, dtype=torch.uint8)
+        step = lambda i: rdna2_ops.fp8_linear(xs[i % sets], wqs[i % sets], sw, out_dtype=torch.bfloat16,
+                                              workspace=ws)
+        metric, flops, launches = f"FP8 e4m3 linear TFLOPS (config 4, M={m})", 2.0 * m * n * k, 2
+        traffic = n * k + n * 4 + m * k * 2 + m * n * 2
+        if m == 1:
+            bound, peak, unit = "hbm", pk["hbm_gbs"], "GB/s"
+        else:
+            bound, peak, unit = "tensor", 2.0 * pk["bf16_tflops"], "TFLOP/s"
+        dtype = "e4m3"
+    else:
+        raise SystemExit(f"unknown workload {name}")
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    value = flops / (ms * 1e-3) / 1e12
+    if bound == "hbm":
+        achieved = traffic / (ms * 1e-3) / 1e9
+    else:
+        achieved = value
+    line = {"workload": name, "metric": metric, "value": round(value, 2), "unit": "TOPS" if dtype == "int8" else "TFLOP/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "dtype": dtype, "data": "synthetic",
+            "config": {"M": m, "N": n, "K": k, "l2": f"weights cycled over {sets} copies"},
+            "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": unit,
+                         "frac": round(achieved / peak, 4), "algorithmic_bytes": traffic,
+                         "peak_source": pk["source"]},
+            "gpu_launches": launches * args.steps, "clocks": clocks.summary(),
+            "device_status": nat.device_status()}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -398,6 +498,10 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload != "c2":
+        if rank == 0:
+            run_workload(args)
         return
     if world > 1:
         import datetime

@@ -120,16 +120,18 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
                     size_t workspace_bytes, void* stream);
 
 /* Split-K workspace bytes b2_w4a16_gemm needs for these sizes (0 = none). */
-size_t b2_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K);
+size_t b2_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int group);
 
 /* W4A16 weight-only GEMM: out[m,n] = sum_k a[m,k] * w[n,k] (+ bias[n]) with
  * w[n,k] = round((u - zu) * s) in the activation's 16-bit type.
  *   a       [M,K] fp16 (a_dtype 1) or bf16 (2), row stride lda, 16-byte rows
- *   wq      [N, ldw] int32 words, unsigned nibble k at bits 4*(k%8) of word k/8
+ *   wq      [N, ldw] int32 words of unsigned nibbles; element k is in word
+ *           k/8 at nibble position (j >> 1) + 4*(j & 1), j = k % 8
+ *           (b2_int4_to_w4a16_words produces this from PackedInt4 words)
  *   scales, zeros  [N, ldsz] in a_dtype; zeros are the integers zu in [0,15]
  *   group   32, 64 or 128; K a multiple of 64 and of group
  *   out     [M,N] in a_dtype, row stride ldo
- *   workspace >= b2_w4a16_workspace_bytes(M, N, K) (split-K partials)
+ *   workspace >= b2_w4a16_workspace_bytes(M, N, K, group) (split-K partials)
  * Replaces int4_linear_a16 / _linear_dot2 (rdna2_ops/int4_weight_gemm_v07.py
  * :540-564, 365-387) in the north-star uint4 + 16-bit scale/zero format. */
 int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* wq, int64_t ldw,
@@ -143,10 +145,10 @@ int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* wq, int64
 int b2_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld, int out_dtype,
                   void* out, int64_t ldo, void* stream);
 
-/* dst = src ^ 0x88888888 over n_words words: converts the reference's signed
- * nibbles (q = u - 8, PackedInt4 at int4_weight_gemm_v07.py:20-46) to the
- * unsigned nibbles b2_w4a16_gemm reads, and back. */
-int b2_int4_flip_nibbles(const void* src, void* dst, int64_t n_words, void* stream);
+/* Converts n_words PackedInt4 words (layout "nk", order "low": signed
+ * nibbles q = u - 8, element j at nibble j; int4_weight_gemm_v07.py:20-46)
+ * into the words b2_w4a16_gemm reads (unsigned nibbles, interleaved). */
+int b2_int4_to_w4a16_words(const void* src, void* dst, int64_t n_words, void* stream);
 
 /* Group INT4 packer with the semantics of pack_int4 / pack_int4_cpu
  * (rdna2_ops/int4_weight_gemm_v07.py:49-82, 413-430): w [N,K] of w_dtype

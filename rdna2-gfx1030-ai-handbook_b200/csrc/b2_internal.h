@@ -53,10 +53,10 @@ cudaError_t run_repack(const void* src, int elem_bytes, int64_t rows, int64_t co
 cudaError_t run_w4a16(const void* a, int a_dtype, int64_t lda, const uint32_t* wq, int64_t ldw,
                       const uint16_t* scales, const uint16_t* zeros, int64_t ldsz, int group,
                       int64_t M, int64_t N, int64_t K, const void* bias, int bias_dtype, void* out,
-                      int64_t ldo, float* partial, size_t partial_bytes, int splits,
-                      cudaStream_t stream);
-int w4a16_splits(int64_t M, int64_t N, int64_t K);
-cudaError_t run_nibble_flip(const uint32_t* src, uint32_t* dst, int64_t n, cudaStream_t stream);
+                      int64_t ldo, float* partial, size_t partial_bytes, cudaStream_t stream);
+void w4a16_plan(int64_t M, int64_t N, int64_t K, int group, int* splits, int* kb_per_split,
+                int* stage_groups);
+cudaError_t run_w4a16_words(const uint32_t* src, uint32_t* dst, int64_t n, cudaStream_t stream);
 cudaError_t run_pack_int4(const void* w, int w_dtype, int64_t ldw_el, int64_t N, int64_t K, int G,
                           int symmetric, int layout_kn, int order_high, int32_t* data, float* scales,
                           int32_t* zeros, int32_t* sums, cudaStream_t stream);

@@ -154,9 +154,10 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
   return static_cast<int>(b2::run_qgemm(kind, q, ldq, w, ldw, p, 0, s));
 }
 
-size_t b2_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K) {
-  if (M <= 0 || N <= 0 || K < 64) return 0;
-  const int splits = b2::w4a16_splits(M, N, K);
+size_t b2_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int group) {
+  if (M <= 0 || N <= 0 || K < 64 || K % 64 || (group != 32 && group != 64 && group != 128)) return 0;
+  int splits = 1, kbps = 1, groups = 1;
+  b2::w4a16_plan(M, N, K, group, &splits, &kbps, &groups);
   return splits > 1 ? static_cast<size_t>(splits) * M * N * 4 : 0;
 }
 
@@ -174,14 +175,13 @@ int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* wq, int64
   if (!aligned16(wq) || (ldw * 4) % 16 || ldw < K / 8) return fail();
   if (ldsz < K / group || ldo < N) return fail();
   if (bias && (bias_dtype < 0 || bias_dtype > 2)) return fail();
-  const int splits = b2::w4a16_splits(M, N, K);
-  if (splits > 1 && (workspace == nullptr || workspace_bytes < static_cast<size_t>(splits) * M * N * 4))
-    return fail();
+  const size_t need = b2_w4a16_workspace_bytes(M, N, K, group);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return fail();
   return static_cast<int>(b2::run_w4a16(a, a_dtype, lda, static_cast<const uint32_t*>(wq), ldw,
                                         static_cast<const uint16_t*>(scales),
                                         static_cast<const uint16_t*>(zeros), ldsz, group, M, N, K, bias,
                                         bias_dtype, out, ldo, static_cast<float*>(workspace),
-                                        workspace_bytes, splits, static_cast<cudaStream_t>(stream)));
+                                        workspace_bytes, static_cast<cudaStream_t>(stream)));
 }
 
 int b2_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld, int out_dtype,
@@ -195,11 +195,11 @@ int b2_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int6
                                              static_cast<cudaStream_t>(stream)));
 }
 
-int b2_int4_flip_nibbles(const void* src, void* dst, int64_t n_words, void* stream) {
+int b2_int4_to_w4a16_words(const void* src, void* dst, int64_t n_words, void* stream) {
   if (n_words < 0) return fail();
   if (n_words == 0) return 0;
   if (!src || !dst) return fail();
-  return static_cast<int>(b2::run_nibble_flip(static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst),
+  return static_cast<int>(b2::run_w4a16_words(static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst),
                                               n_words, static_cast<cudaStream_t>(stream)));
 }
 

@@ -6,12 +6,14 @@
 // weight as ((q - z).to(fp32) * s).to(fp16) inside the K loop and
 // accumulates fp16 x fp16 products in fp32.
 //
-// Weight format (the north-star uint4 layout): eight unsigned nibbles per
-// 32-bit word, element k at bits 4*(k%8) of word k/8 of its row ([N, K/8]);
-// scales and zero-points [N, K/group] in the activation's 16-bit type (zero
+// Weight format (the north-star uint4 layout, nibbles interleaved for the
+// kernel): eight unsigned nibbles per 32-bit word, word k/8 of its row
+// ([N, K/8]); element j = k % 8 sits at nibble position (j >> 1) + 4 * (j & 1),
+// so masking nibbles {i, i+4} yields elements (2i, 2i+1) in K order.  Scales
+// and zero points are [N, K/group] in the activation's 16-bit type (zero
 // points are the integers zu in [0,15]).  The reference's PackedInt4 stores
-// signed nibbles q = u - 8 and zeros zu - 8; the value q - z = u - zu is the
-// same, and the host converter flips bit 3 of every nibble.
+// signed nibbles q = u - 8 in natural order and zeros zu - 8; the value
+// q - z = u - zu is the same, and b2_int4_to_w4a16_words converts the words.
 //
 // B200 design: swap-AB.  The dequantized weight tile is the 128-row A operand
 // of tcgen05.mma kind::f16 and the tokens are its N dimension (32..256), so
@@ -42,6 +44,7 @@ struct W4Params {
   int64_t ldo;
   float* partial;          // [splits, M, N] fp32 (splits > 1)
   int splits, kb_per_split, num_kb, tiles_t;
+  int stage_groups;        // groups staged in shared memory per CTA (>= groups of a split)
   int* status;
 };
 
@@ -49,27 +52,23 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// One 32-bit word of 8 nibbles -> 8 16-bit weights (one 16-byte chunk) in K order.
+// One 32-bit word of 8 interleaved nibbles -> 8 16-bit weights (one 16-byte
+// chunk) in K order.
 template <bool BF16>
 __device__ __forceinline__ uint4 dequant_word(uint32_t w, uint32_t zz, uint32_t ss) {
   constexpr uint32_t kBias = BF16 ? 0x43004300u : 0x64006400u;  // 128+u (bf16), 1024+u (fp16)
-  const uint32_t t0 = (w & 0x000F000Fu) | kBias;          // (u0, u4)
-  const uint32_t t1 = ((w >> 4) & 0x000F000Fu) | kBias;   // (u1, u5)
-  const uint32_t t2 = ((w >> 8) & 0x000F000Fu) | kBias;   // (u2, u6)
-  const uint32_t t3 = ((w >> 12) & 0x000F000Fu) | kBias;  // (u3, u7)
-  uint32_t p[4] = {__byte_perm(t0, t1, 0x5410), __byte_perm(t2, t3, 0x5410),
-                   __byte_perm(t0, t1, 0x7632), __byte_perm(t2, t3, 0x7632)};
   uint32_t r[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
+    const uint32_t t = ((w >> (4 * i)) & 0x000F000Fu) | kBias;   // elements (2i, 2i+1)
     if constexpr (BF16) {
       // (128+u) - (128+zu) is exact; one rounding in the product.
-      const __nv_bfloat162 d = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&p[i]),
+      const __nv_bfloat162 d = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&t),
                                        *reinterpret_cast<const __nv_bfloat162*>(&zz));
       const __nv_bfloat162 v = __hmul2(d, *reinterpret_cast<const __nv_bfloat162*>(&ss));
       r[i] = *reinterpret_cast<const uint32_t*>(&v);
     } else {
-      const __half2 d = __hsub2(*reinterpret_cast<const __half2*>(&p[i]),
+      const __half2 d = __hsub2(*reinterpret_cast<const __half2*>(&t),
                                 *reinterpret_cast<const __half2*>(&zz));
       const __half2 v = __hmul2(d, *reinterpret_cast<const __half2*>(&ss));
       r[i] = *reinterpret_cast<const uint32_t*>(&v);
@@ -111,13 +110,17 @@ struct W4Smem {
   static constexpr int kOffBar = kOffRaw + STAGES * kRawBytes;
   static constexpr int kNumBars = 3 * STAGES + 1;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
-  static constexpr int kAlloc = kOffMisc + 16 + 1024;
+  static constexpr int kOffGroups = kOffMisc + 16;     // [2][128][stage_groups] u32, dynamic
+  static constexpr int kFixed = kOffGroups + 1024;     // + group staging at launch
   static constexpr uint32_t kTmemCols = BT < 32 ? 32 : BT;
-  static_assert(kAlloc <= 232448, "shared memory budget");
+  static constexpr int kMaxGroups = (232448 - kFixed) / (2 * 128 * 4);
+  static_assert(kMaxGroups >= 8, "shared memory budget");
 };
 
+constexpr int kW4Threads = 320;  // producer, MMA, 8 transform warps (4 of them also epilogue)
+
 template <bool BF16, int BT, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kW4Threads, 1)
     w4a16_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_a,
                  const W4Params p) {
   using L = W4Smem<BT, STAGES>;
@@ -144,7 +147,7 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_raw[s], 1);
-      mbar_init(&full_xf[s], 4);
+      mbar_init(&full_xf[s], 8);
       mbar_init(&empty[s], 1);
     }
     mbar_init(&tfull[0], 1);
@@ -219,30 +222,42 @@ __global__ void __launch_bounds__(192, 1)
       if (ok) umma_commit(&tfull[0]);
     }
   } else {
-    // ---- transform: thread r dequantizes weight row n0 + r of every k-block
-    const int r = threadIdx.x - 64;  // 0..127
+    // ---- transform: 256 threads; thread (r, h) dequantizes words 4h..4h+3
+    // (elements 32h..32h+31) of weight row n0 + r of every k-block.
+    const int t = threadIdx.x - 64;  // 0..255
+    const int r = t & 127, h = t >> 7;
     const int n = n0 + r;
+    const int g_first = (kb0 * 64) / p.group;
+    const int ng = p.stage_groups;
+    uint32_t* s_zz = reinterpret_cast<uint32_t*>(smem + L::kOffGroups);
+    uint32_t* s_ss = s_zz + 128 * ng;
+    // Stage this CTA's (128 rows x ng groups) zero/scale operands once.
+    for (int i = t; i < 128 * ng; i += 256) {
+      const int rr = i / ng, gg = i % ng;
+      const int g = g_first + gg;
+      uint32_t zz = 0, ss = 0;
+      if (g < p.K / p.group) group_operands<BF16>(p, n0 + rr, g, zz, ss);
+      s_zz[rr * ng + gg] = zz;
+      s_ss[rr * ng + gg] = ss;
+    }
+    named_bar_sync(1, 256);
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
     for (int i = 0; i < nkb && ok; ++i) {
       const int kb = kb0 + i;
-      // scale / zero operands for the (up to two) groups this k-block touches
-      uint32_t zz0, ss0, zz1, ss1;
-      const int g0 = (kb * 64) / p.group, g1 = (kb * 64 + 32) / p.group;
-      group_operands<BF16>(p, n, g0, zz0, ss0);
-      group_operands<BF16>(p, n, g1, zz1, ss1);
+      const int gl = (kb * 64 + h * 32) / p.group - g_first;  // 32 elements never straddle a group
+      const uint32_t zz = s_zz[r * ng + gl], ss = s_ss[r * ng + gl];
       ok = mbar_wait(&full_raw[stage], phase, abort_flag, kSiteTransform, p.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      const uint4* raw = reinterpret_cast<const uint4*>(smem + L::kOffRaw + stage * L::kRawBytes + r * 32);
-      const uint4 w0 = raw[0], w1 = raw[1];
-      const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const uint4 w = *reinterpret_cast<const uint4*>(smem + L::kOffRaw + stage * L::kRawBytes + r * 32 + h * 16);
+      const uint32_t words[4] = {w.x, w.y, w.z, w.w};
       uint8_t* xf = smem + L::kOffXf + stage * L::kXfBytes + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = dequant_word<BF16>(words[c], c < 4 ? zz0 : zz1, c < 4 ? ss0 : ss1);
-        *reinterpret_cast<uint4*>(xf + ((c ^ (r & 7)) << 4)) = v;
+      for (int j = 0; j < 4; ++j) {
+        const int c = 4 * h + j;
+        *reinterpret_cast<uint4*>(xf + ((c ^ (r & 7)) << 4)) = dequant_word<BF16>(words[j], zz, ss);
       }
       fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
       __syncwarp();
@@ -252,8 +267,9 @@ __global__ void __launch_bounds__(192, 1)
         phase ^= 1u;
       }
     }
+    (void)n;
     // ---- epilogue: TMEM lane = weight row, column = token
-    if (ok && nkb > 0) {
+    if (ok && nkb > 0 && warp < 6) {
       const int quarter = warp & 3;
       bool done = mbar_wait(&tfull[0], 0, abort_flag, kSiteEpilogue, p.status);
       done = __all_sync(0xffffffffu, done);
@@ -311,11 +327,17 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int spli
   *o = BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(acc)) : __half_as_ushort(__float2half_rn(acc));
 }
 
-// Flip bit 3 of every nibble: signed-nibble words (reference PackedInt4,
-// q = u - 8) <-> unsigned-nibble words (u).
-__global__ void nibble_flip_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst, int64_t n) {
+// Reference PackedInt4 words (signed nibbles q = u - 8, element j at nibble
+// j) -> kernel words (unsigned nibbles u, element j at nibble
+// (j >> 1) + 4 * (j & 1)).
+__global__ void w4a16_words_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst, int64_t n) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i < n) dst[i] = src[i] ^ 0x88888888u;
+  if (i >= n) return;
+  const uint32_t u = src[i] ^ 0x88888888u;
+  uint32_t w = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) w |= ((u >> (4 * j)) & 15u) << (4 * ((j >> 1) + 4 * (j & 1)));
+  dst[i] = w;
 }
 
 // Group INT4 packer, one thread per (row, group): the restated semantics of
@@ -438,8 +460,11 @@ static cudaError_t launch_w4(const void* a, int64_t lda, W4Params p, cudaStream_
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64) return cudaErrorInvalidDevice;
+  if (p.stage_groups > L::kMaxGroups) return cudaErrorInvalidValue;
+  const int smem = L::kFixed + 2 * 128 * 4 * p.stage_groups;
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L::kFixed + 2 * 128 * 4 * L::kMaxGroups);
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
@@ -452,15 +477,46 @@ static cudaError_t launch_w4(const void* a, int64_t lda, W4Params p, cudaStream_
   if (e != cudaSuccess) return e;
   p.tiles_t = (p.M + BT - 1) / BT;
   dim3 grid((p.N + 127) / 128, p.tiles_t, p.splits);
-  kernel<<<grid, 192, L::kAlloc, stream>>>(mw, ma, p);
+  kernel<<<grid, kW4Threads, smem, stream>>>(mw, ma, p);
   return cudaGetLastError();
+}
+
+// Token tile for M tokens (each with its own ring depth below).
+static int w4_bt(int64_t M) { return M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
+static int w4_max_groups(int bt) {
+  return bt == 32 ? W4Smem<32, 4>::kMaxGroups : bt == 64 ? W4Smem<64, 6>::kMaxGroups
+       : bt == 128 ? W4Smem<128, 5>::kMaxGroups : W4Smem<256, 3>::kMaxGroups;
+}
+
+// Split count and staged groups per CTA: fill the machine for small token
+// counts (at least 4 k-blocks per split) and keep a split's scale/zero
+// operands within the shared-memory staging area.
+void w4a16_plan(int64_t M, int64_t N, int64_t K, int group, int* splits_out, int* kbps_out,
+                int* groups_out) {
+  const int bt = w4_bt(M);
+  const int64_t num_kb = K / 64;
+  const int64_t ctas = ((N + 127) / 128) * ((M + bt - 1) / bt);
+  int64_t s = (2 * static_cast<int64_t>(device_sm_count()) + ctas - 1) / ctas;
+  const int64_t max_s = num_kb / 4 > 0 ? num_kb / 4 : 1;
+  if (s > max_s) s = max_s;
+  if (s < 1) s = 1;
+  for (;;) {
+    const int64_t kbps = (num_kb + s - 1) / s;
+    const int64_t groups = kbps * 64 / group + 2;
+    if (groups <= w4_max_groups(bt) || s >= num_kb) {
+      *splits_out = static_cast<int>((num_kb + kbps - 1) / kbps);
+      *kbps_out = static_cast<int>(kbps);
+      *groups_out = static_cast<int>(groups);
+      return;
+    }
+    ++s;
+  }
 }
 
 cudaError_t run_w4a16(const void* a, int a_dtype, int64_t lda, const uint32_t* wq, int64_t ldw,
                       const uint16_t* scales, const uint16_t* zeros, int64_t ldsz, int group,
                       int64_t M, int64_t N, int64_t K, const void* bias, int bias_dtype, void* out,
-                      int64_t ldo, float* partial, size_t partial_bytes, int splits,
-                      cudaStream_t stream) {
+                      int64_t ldo, float* partial, size_t partial_bytes, cudaStream_t stream) {
   if (M == 0 || N == 0) return cudaSuccess;
   W4Params p{};
   p.M = static_cast<int>(M);
@@ -478,39 +534,25 @@ cudaError_t run_w4a16(const void* a, int a_dtype, int64_t lda, const uint32_t* w
   p.ldo = ldo;
   p.num_kb = static_cast<int>(K / 64);
   p.status = status_word_ptr();
-  if (splits < 1) splits = 1;
-  if (splits > p.num_kb) splits = p.num_kb;
-  p.kb_per_split = (p.num_kb + splits - 1) / splits;
-  p.splits = (p.num_kb + p.kb_per_split - 1) / p.kb_per_split;
+  w4a16_plan(M, N, K, group, &p.splits, &p.kb_per_split, &p.stage_groups);
   if (p.splits > 1) {
     if (partial == nullptr || partial_bytes < static_cast<size_t>(p.splits) * M * N * 4)
       return cudaErrorInvalidValue;
     p.partial = partial;
   }
   const bool bf = a_dtype == kBF16;
+  const int bt = w4_bt(M);
   cudaError_t e;
-  if (M <= 32) e = bf ? launch_w4<true, 32, 4>(a, lda, p, stream) : launch_w4<false, 32, 4>(a, lda, p, stream);
-  else if (M <= 64) e = bf ? launch_w4<true, 64, 7>(a, lda, p, stream) : launch_w4<false, 64, 7>(a, lda, p, stream);
-  else if (M <= 128) e = bf ? launch_w4<true, 128, 6>(a, lda, p, stream) : launch_w4<false, 128, 6>(a, lda, p, stream);
-  else e = bf ? launch_w4<true, 256, 4>(a, lda, p, stream) : launch_w4<false, 256, 4>(a, lda, p, stream);
+  if (bt == 32) e = bf ? launch_w4<true, 32, 4>(a, lda, p, stream) : launch_w4<false, 32, 4>(a, lda, p, stream);
+  else if (bt == 64) e = bf ? launch_w4<true, 64, 6>(a, lda, p, stream) : launch_w4<false, 64, 6>(a, lda, p, stream);
+  else if (bt == 128) e = bf ? launch_w4<true, 128, 5>(a, lda, p, stream) : launch_w4<false, 128, 5>(a, lda, p, stream);
+  else e = bf ? launch_w4<true, 256, 3>(a, lda, p, stream) : launch_w4<false, 256, 3>(a, lda, p, stream);
   if (e != cudaSuccess || p.splits == 1) return e;
   const int64_t total = M * N;
   const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
   if (bf) splitk_reduce_kernel<true><<<blocks, 256, 0, stream>>>(partial, p.splits, p.M, p.N, bias, bias_dtype, out, ldo);
   else splitk_reduce_kernel<false><<<blocks, 256, 0, stream>>>(partial, p.splits, p.M, p.N, bias, bias_dtype, out, ldo);
   return cudaGetLastError();
-}
-
-// Split count that fills the machine for small token counts (K stays >= 4
-// k-blocks per split); large M uses one split.
-int w4a16_splits(int64_t M, int64_t N, int64_t K) {
-  const int64_t bt = M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
-  const int64_t ctas = ((N + 127) / 128) * ((M + bt - 1) / bt);
-  const int64_t want = (2 * static_cast<int64_t>(device_sm_count()) + ctas - 1) / ctas;
-  int64_t s = want < 1 ? 1 : want;
-  const int64_t max_s = (K / 64) / 4 > 0 ? (K / 64) / 4 : 1;
-  if (s > max_s) s = max_s;
-  return static_cast<int>(s);
 }
 
 cudaError_t run_pack_int4(const void* w, int w_dtype, int64_t ldw_el, int64_t N, int64_t K, int G,
@@ -534,9 +576,9 @@ cudaError_t run_unpack_int4(const int32_t* data, int layout_kn, int order_high, 
   return cudaGetLastError();
 }
 
-cudaError_t run_nibble_flip(const uint32_t* src, uint32_t* dst, int64_t n, cudaStream_t stream) {
+cudaError_t run_w4a16_words(const uint32_t* src, uint32_t* dst, int64_t n, cudaStream_t stream) {
   if (n == 0) return cudaSuccess;
-  nibble_flip_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(src, dst, n);
+  w4a16_words_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(src, dst, n);
   return cudaGetLastError();
 }
 

@@ -54,8 +54,9 @@ class PackedInt4:
 
 @dataclass
 class W4A16Weight:
-    """B200 weight format: words [N, K/8] int32 of unsigned nibbles (element k
-    at bits 4*(k%8)), scales and zero points [N, K/group] in `dtype`."""
+    """B200 weight format: words [N, K/8] int32 of unsigned nibbles, element
+    j = k % 8 of word k/8 at nibble position (j >> 1) + 4*(j & 1); scales and
+    zero points [N, K/group] in `dtype`."""
     words: torch.Tensor
     scales: torch.Tensor
     zeros: torch.Tensor
@@ -191,8 +192,8 @@ def prepare_w4a16(p, dtype=torch.bfloat16):
         words = rev.to(torch.int32)
     words = words.contiguous()
     flipped = torch.empty_like(words)
-    nat.check(nat.library().b2_int4_flip_nibbles(words.data_ptr(), flipped.data_ptr(), words.numel(),
-                                                 nat.stream_ptr(words.device)), "b2_int4_flip_nibbles")
+    nat.check(nat.library().b2_int4_to_w4a16_words(words.data_ptr(), flipped.data_ptr(), words.numel(),
+                                                   nat.stream_ptr(words.device)), "b2_int4_to_w4a16_words")
     zu = (p.zeros + 8).to(dtype)            # integers 0..15, exact in 16 bits
     return W4A16Weight(flipped, p.scales.to(dtype).contiguous(), zu.contiguous(), p.n, p.k,
                        p.group_size, dtype)
@@ -216,7 +217,7 @@ def w4a16_gemm(a, wt, bias=None, *, workspace=None):
     m = a.shape[0]
     out = torch.empty((m, wt.n), device=dev, dtype=a.dtype)
     lib = nat.library()
-    need = lib.b2_w4a16_workspace_bytes(m, wt.n, wt.k)
+    need = lib.b2_w4a16_workspace_bytes(m, wt.n, wt.k, wt.group_size)
     if need and (workspace is None or workspace.numel() < need):
         workspace = torch.empty(need, device=dev, dtype=torch.uint8)
     nat.check(lib.b2_w4a16_gemm(

@@ -112,7 +112,7 @@ def test_w4a16_deterministic_split_k():
     w = torch.randn((4096, 4096), generator=gen, device="cuda") * 0.02
     wt = i4.quantize_w4a16(w, group_size=128, dtype=dtype)
     a = torch.randn((8, 4096), generator=gen, device="cuda").to(dtype)
-    assert nat.library().b2_w4a16_workspace_bytes(8, 4096, 4096) > 0  # split-K engaged
+    assert nat.library().b2_w4a16_workspace_bytes(8, 4096, 4096, 128) > 0  # split-K engaged
     y1, y2 = i4.w4a16_gemm(a, wt), i4.w4a16_gemm(a, wt)
     assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
 
