@@ -119,36 +119,55 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
                     void* out, int out_dtype, int64_t ldc, void* workspace,
                     size_t workspace_bytes, void* stream);
 
-/* Split-K workspace bytes b2_w4a16_gemm needs for these sizes (0 = none). */
+/* W4A16 weight format ("tiles"), a caller-owned pack of one PackedInt4
+ * (the reference keeps packs caller-owned, int4_weight_gemm_v07.py:4-6):
+ *   tiles   u32 [T][K/64][128][8], T = ceil(N/128): one 4 KiB chunk per
+ *           (128-row tile, 64-element k-block), unsigned nibbles u = q + 8;
+ *           element j = k % 8 of a word at nibble (j >> 1) + 4*(j & 1)
+ *   groups  u32 [T][K/group][128]: low 16 bits the scale, high 16 bits the
+ *           zero point zu (integer 0..15), both in the activation's type
+ * Rows past N are zero.  The byte sizes of the two buffers: */
+size_t b2_w4a16_tiles_bytes(int64_t N, int64_t K);
+size_t b2_w4a16_groups_bytes(int64_t N, int64_t K, int group);
+
+/* PackedInt4 (int4_weight_gemm_v07.py:20-46: data int32 signed nibbles
+ * q = u - 8, layout_kn 0 "nk" [N,K/8] / 1 "kn" [K/8,N], order_high 1 puts
+ * element 0 in the top nibble; scales fp32 [N,K/group]; zeros int32
+ * zu - 8 [N,K/group]) -> tiles + groups for activations of dtype (1 fp16,
+ * 2 bf16).  Lossless except the scale's round-to-nearest-even cast to
+ * 16 bits, the one rounding the 16-bit scale format implies. */
+int b2_w4a16_prepare(const void* data, int layout_kn, int order_high, const float* scales,
+                     const void* zeros, int64_t N, int64_t K, int group, int dtype, void* tiles,
+                     void* groups, void* stream);
+
+/* Workspace bytes b2_w4a16_gemm needs for these sizes on the current device
+ * (0 = none; M <= 32 needs one, sized by the SM count).  Its first 4 KiB
+ * are arrival counters: zero-fill them once before the first use; every
+ * completed call leaves them zero again, for any later shape (after a call
+ * that left a nonzero b2_device_status, zero them again). */
 size_t b2_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int group);
 
 /* W4A16 weight-only GEMM: out[m,n] = sum_k a[m,k] * w[n,k] (+ bias[n]) with
  * w[n,k] = round((u - zu) * s) in the activation's 16-bit type.
  *   a       [M,K] fp16 (a_dtype 1) or bf16 (2), row stride lda, 16-byte rows
- *   wq      [N, ldw] int32 words of unsigned nibbles; element k is in word
- *           k/8 at nibble position (j >> 1) + 4*(j & 1), j = k % 8
- *           (b2_int4_to_w4a16_words produces this from PackedInt4 words)
- *   scales, zeros  [N, ldsz] in a_dtype; zeros are the integers zu in [0,15]
+ *   tiles, groups  from b2_w4a16_prepare (16-byte aligned)
  *   group   32, 64 or 128; K a multiple of 64 and of group
- *   out     [M,N] in a_dtype, row stride ldo
- *   workspace >= b2_w4a16_workspace_bytes(M, N, K, group) (split-K partials)
- * Replaces int4_linear_a16 / _linear_dot2 (rdna2_ops/int4_weight_gemm_v07.py
- * :540-564, 365-387) in the north-star uint4 + 16-bit scale/zero format. */
-int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* wq, int64_t ldw,
-                  const void* scales, const void* zeros, int64_t ldsz, int group, int64_t M,
-                  int64_t N, int64_t K, const void* bias, int bias_dtype, void* out, int64_t ldo,
-                  void* workspace, size_t workspace_bytes, void* stream);
+ *   out     [M,N] in a_dtype, row stride ldo; bias [N] of bias_dtype or NULL
+ *   workspace >= b2_w4a16_workspace_bytes(M, N, K, group), 16-byte aligned,
+ *           zero-filled before its first use (see above); calls sharing
+ *           one workspace must not overlap on the GPU
+ * Results are deterministic run to run on one device.  Replaces
+ * int4_linear_a16 / _linear_dot2 (rdna2_ops/int4_weight_gemm_v07.py
+ * :540-564, 365-387) with uint4 + 16-bit scales/zero points. */
+int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* tiles, const void* groups,
+                  int group, int64_t M, int64_t N, int64_t K, const void* bias, int bias_dtype,
+                  void* out, int64_t ldo, void* workspace, size_t workspace_bytes, void* stream);
 
 /* Exact fp8 decode (rdna2_ops/fp8_weight_gemm_v06.py:22-46, 109-124):
  * w [rows, cols] of fp8_dtype (4 e4m3fn, 5 e5m2), row stride ld bytes ->
  * out of out_dtype (0 fp32, 1 fp16), row stride ldo elements. */
 int b2_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld, int out_dtype,
                   void* out, int64_t ldo, void* stream);
-
-/* Converts n_words PackedInt4 words (layout "nk", order "low": signed
- * nibbles q = u - 8, element j at nibble j; int4_weight_gemm_v07.py:20-46)
- * into the words b2_w4a16_gemm reads (unsigned nibbles, interleaved). */
-int b2_int4_to_w4a16_words(const void* src, void* dst, int64_t n_words, void* stream);
 
 /* Group INT4 packer with the semantics of pack_int4 / pack_int4_cpu
  * (rdna2_ops/int4_weight_gemm_v07.py:49-82, 413-430): w [N,K] of w_dtype

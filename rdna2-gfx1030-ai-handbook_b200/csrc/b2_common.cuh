@@ -25,6 +25,7 @@ enum : int {
   kSiteMmaTmem = 3,
   kSiteEpilogue = 4,
   kSiteTransform = 5,
+  kSiteFixup = 6,
 };
 
 // Longest time any single mbarrier wait may take before the CTA abandons its

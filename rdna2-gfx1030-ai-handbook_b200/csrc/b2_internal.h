@@ -49,14 +49,17 @@ cudaError_t run_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t c
 cudaError_t run_repack(const void* src, int elem_bytes, int64_t rows, int64_t cols, int64_t s_row,
                        int64_t s_col, void* dst, int64_t ldd, cudaStream_t stream);
 
-// W4A16 (see w4a16.cu); `partial` holds splits * M * N fp32 when splits > 1.
-cudaError_t run_w4a16(const void* a, int a_dtype, int64_t lda, const uint32_t* wq, int64_t ldw,
-                      const uint16_t* scales, const uint16_t* zeros, int64_t ldsz, int group,
-                      int64_t M, int64_t N, int64_t K, const void* bias, int bias_dtype, void* out,
-                      int64_t ldo, float* partial, size_t partial_bytes, cudaStream_t stream);
-void w4a16_plan(int64_t M, int64_t N, int64_t K, int group, int* splits, int* kb_per_split,
-                int* stage_groups);
-cudaError_t run_w4a16_words(const uint32_t* src, uint32_t* dst, int64_t n, cudaStream_t stream);
+// W4A16 on the tiled weight format (see w4a16.cu); `partial` holds the
+// stream-K slots, w4a16_workspace(M, N, K) bytes (0 when not needed).
+cudaError_t run_w4a16(const void* a, int a_dtype, int64_t lda, const void* tiles, const void* groups, int group,
+                      int64_t M, int64_t N, int64_t K, const void* bias, int bias_dtype, void* out, int64_t ldo,
+                      float* partial, size_t partial_bytes, cudaStream_t stream);
+size_t w4a16_workspace(int64_t M, int64_t N, int64_t K);
+size_t w4a16_tiles_bytes(int64_t N, int64_t K);
+size_t w4a16_groups_bytes(int64_t N, int64_t K, int group);
+cudaError_t run_w4a16_prepare(const uint32_t* data, int layout_kn, int order_high, const float* scales,
+                              const int32_t* zeros, int64_t N, int64_t K, int group, int dtype, uint32_t* tiles,
+                              uint32_t* groups, cudaStream_t stream);
 cudaError_t run_pack_int4(const void* w, int w_dtype, int64_t ldw_el, int64_t N, int64_t K, int G,
                           int symmetric, int layout_kn, int order_high, int32_t* data, float* scales,
                           int32_t* zeros, int32_t* sums, cudaStream_t stream);

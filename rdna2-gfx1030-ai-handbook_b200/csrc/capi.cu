@@ -154,34 +154,54 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
   return static_cast<int>(b2::run_qgemm(kind, q, ldq, w, ldw, p, 0, s));
 }
 
-size_t b2_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int group) {
-  if (M <= 0 || N <= 0 || K < 64 || K % 64 || (group != 32 && group != 64 && group != 128)) return 0;
-  int splits = 1, kbps = 1, groups = 1;
-  b2::w4a16_plan(M, N, K, group, &splits, &kbps, &groups);
-  return splits > 1 ? static_cast<size_t>(splits) * M * N * 4 : 0;
+namespace {
+bool w4_shape_ok(int64_t N, int64_t K, int group) {
+  if (N <= 0 || K < 64 || K % 64 || N > INT32_MAX || K > INT32_MAX) return false;
+  if (group != 32 && group != 64 && group != 128) return false;
+  return K % group == 0;
+}
+}  // namespace
+
+size_t b2_w4a16_tiles_bytes(int64_t N, int64_t K) {
+  return w4_shape_ok(N, K, 64) ? b2::w4a16_tiles_bytes(N, K) : 0;
 }
 
-int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* wq, int64_t ldw,
-                  const void* scales, const void* zeros, int64_t ldsz, int group, int64_t M, int64_t N,
-                  int64_t K, const void* bias, int bias_dtype, void* out, int64_t ldo, void* workspace,
-                  size_t workspace_bytes, void* stream) {
+size_t b2_w4a16_groups_bytes(int64_t N, int64_t K, int group) {
+  return w4_shape_ok(N, K, group) ? b2::w4a16_groups_bytes(N, K, group) : 0;
+}
+
+int b2_w4a16_prepare(const void* data, int layout_kn, int order_high, const float* scales, const void* zeros,
+                     int64_t N, int64_t K, int group, int dtype, void* tiles, void* groups, void* stream) {
+  if (!w4_shape_ok(N, K, group) || (dtype != b2::kF16 && dtype != b2::kBF16)) return fail();
+  if (N * K >= (int64_t{1} << 31)) return fail();
+  if (!data || !scales || !zeros || !tiles || !groups) return fail();
+  return static_cast<int>(b2::run_w4a16_prepare(static_cast<const uint32_t*>(data), layout_kn != 0,
+                                                order_high != 0, scales, static_cast<const int32_t*>(zeros), N, K,
+                                                group, dtype, static_cast<uint32_t*>(tiles),
+                                                static_cast<uint32_t*>(groups), static_cast<cudaStream_t>(stream)));
+}
+
+size_t b2_w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int group) {
+  if (M <= 0 || M > INT32_MAX || !w4_shape_ok(N, K, group)) return 0;
+  return b2::w4a16_workspace(M, N, K);
+}
+
+int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* tiles, const void* groups, int group,
+                  int64_t M, int64_t N, int64_t K, const void* bias, int bias_dtype, void* out, int64_t ldo,
+                  void* workspace, size_t workspace_bytes, void* stream) {
   if (a_dtype != b2::kF16 && a_dtype != b2::kBF16) return fail();
-  if (M < 0 || N < 0 || K < 64 || K % 64 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail();
-  if (group != 32 && group != 64 && group != 128) return fail();
-  if (K % group) return fail();
-  if (M == 0 || N == 0) return 0;
-  if (!a || !wq || !scales || !zeros || !out) return fail();
+  if (M < 0 || N < 0 || M > INT32_MAX || M * N >= (int64_t{1} << 31)) return fail();
+  if (M == 0 || N == 0) return K >= 64 && K % 64 == 0 ? 0 : fail();
+  if (!w4_shape_ok(N, K, group)) return fail();
+  if (!a || !tiles || !groups || !out) return fail();
   if (!aligned16(a) || (lda * 2) % 16 || lda < K) return fail();
-  if (!aligned16(wq) || (ldw * 4) % 16 || ldw < K / 8) return fail();
-  if (ldsz < K / group || ldo < N) return fail();
+  if (!aligned16(tiles) || !aligned16(groups) || ldo < N) return fail();
   if (bias && (bias_dtype < 0 || bias_dtype > 2)) return fail();
   const size_t need = b2_w4a16_workspace_bytes(M, N, K, group);
-  if (need > 0 && (workspace == nullptr || workspace_bytes < need)) return fail();
-  return static_cast<int>(b2::run_w4a16(a, a_dtype, lda, static_cast<const uint32_t*>(wq), ldw,
-                                        static_cast<const uint16_t*>(scales),
-                                        static_cast<const uint16_t*>(zeros), ldsz, group, M, N, K, bias,
-                                        bias_dtype, out, ldo, static_cast<float*>(workspace),
-                                        workspace_bytes, static_cast<cudaStream_t>(stream)));
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) return fail();
+  return static_cast<int>(b2::run_w4a16(a, a_dtype, lda, tiles, groups, group, M, N, K, bias, bias_dtype, out,
+                                        ldo, static_cast<float*>(workspace), workspace_bytes,
+                                        static_cast<cudaStream_t>(stream)));
 }
 
 int b2_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld, int out_dtype,
@@ -193,14 +213,6 @@ int b2_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int6
   if (!w || !out) return fail();
   return static_cast<int>(b2::run_fp8_decode(w, fp8_dtype, rows, cols, ld, out_dtype, out, ldo,
                                              static_cast<cudaStream_t>(stream)));
-}
-
-int b2_int4_to_w4a16_words(const void* src, void* dst, int64_t n_words, void* stream) {
-  if (n_words < 0) return fail();
-  if (n_words == 0) return 0;
-  if (!src || !dst) return fail();
-  return static_cast<int>(b2::run_w4a16_words(static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst),
-                                              n_words, static_cast<cudaStream_t>(stream)));
 }
 
 int b2_pack_int4(const void* w, int w_dtype, int64_t ldw, int64_t N, int64_t K, int group, int symmetric,

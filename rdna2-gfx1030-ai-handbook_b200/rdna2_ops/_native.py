@@ -42,9 +42,11 @@ SIGNATURES = {
     "b2_quant_linear": ([_int, _p, _int, _i64, _i64, _i64, _int, _p, _i64, _i64, _p, _i64, _p,
                          _int, _int, _p, _int, _i64, _p, _size, _p], _int),
     "b2_w4a16_workspace_bytes": ([_i64, _i64, _i64, _int], _size),
-    "b2_w4a16_gemm": ([_p, _int, _i64, _p, _i64, _p, _p, _i64, _int, _i64, _i64, _i64, _p, _int, _p,
-                       _i64, _p, _size, _p], _int),
-    "b2_int4_to_w4a16_words": ([_p, _p, _i64, _p], _int),
+    "b2_w4a16_gemm": ([_p, _int, _i64, _p, _p, _int, _i64, _i64, _i64, _p, _int, _p, _i64, _p, _size,
+                       _p], _int),
+    "b2_w4a16_tiles_bytes": ([_i64, _i64], _size),
+    "b2_w4a16_groups_bytes": ([_i64, _i64, _int], _size),
+    "b2_w4a16_prepare": ([_p, _int, _int, _p, _p, _i64, _i64, _int, _int, _p, _p, _p], _int),
     "b2_fp8_decode": ([_p, _int, _i64, _i64, _i64, _int, _p, _i64, _p], _int),
     "b2_pack_int4": ([_p, _int, _i64, _i64, _i64, _int, _int, _int, _int, _p, _p, _p, _p, _p], _int),
     "b2_unpack_int4": ([_p, _int, _int, _p, _p, _i64, _i64, _int, _int, _p, _p], _int),

@@ -7,12 +7,13 @@ packs, no hidden cache.  `PackedInt4` keeps the reference's fields and
 encodings (signed nibbles q, fp32 scales, int32 zeros = zu - 8, int32 sums,
 layouts "nk"/"kn", nibble orders "low"/"high").
 
-The B200 kernel (csrc/w4a16.cu) reads the north-star format instead --
-unsigned nibbles u = q + 8, 16-bit scales and zero points zu in the
-activation dtype -- held in a caller-owned `W4A16Weight` that
-`prepare_w4a16` builds from a PackedInt4 (the nibble flip is lossless; the
-scale cast to 16 bits is the one rounding, exactly as the north star states).
-`int4_linear_a16` accepts either; a PackedInt4 is converted per call.
+The B200 kernel (csrc/w4a16.cu) reads uint4 weights with 16-bit scales and
+zero points zu in the activation dtype, stored as 4 KiB (128-row x 64-K)
+tiles so that each CTA streams one contiguous byte range.  `prepare_w4a16`
+builds that caller-owned `W4A16Weight` from a PackedInt4 on the device (the
+nibble flip u = q + 8 and zu = z + 8 are lossless; the scale cast to 16 bits
+is the one rounding).  `int4_linear_a16` accepts either; a PackedInt4 is
+converted per call.
 """
 from __future__ import annotations
 
@@ -54,12 +55,13 @@ class PackedInt4:
 
 @dataclass
 class W4A16Weight:
-    """B200 weight format: words [N, K/8] int32 of unsigned nibbles, element
-    j = k % 8 of word k/8 at nibble position (j >> 1) + 4*(j & 1); scales and
-    zero points [N, K/group] in `dtype`."""
-    words: torch.Tensor
-    scales: torch.Tensor
-    zeros: torch.Tensor
+    """B200 weight format (include/b2_qlinear.h, b2_w4a16_prepare):
+    `tiles` int32 [T, K/64, 128, 8] with T = ceil(N/128) -- unsigned nibbles,
+    element j = k % 8 of a word at nibble (j >> 1) + 4*(j & 1); `groups`
+    int32 [T, K/group, 128] -- low half the scale, high half the zero point
+    zu, both in `dtype`.  Rows past N are zero."""
+    tiles: torch.Tensor
+    groups: torch.Tensor
     n: int
     k: int
     group_size: int
@@ -67,7 +69,11 @@ class W4A16Weight:
 
     @property
     def bytes(self):
-        return sum(t.numel() * t.element_size() for t in (self.words, self.scales, self.zeros))
+        return sum(t.numel() * t.element_size() for t in (self.tiles, self.groups))
+
+    def clone(self):
+        return W4A16Weight(self.tiles.clone(), self.groups.clone(), self.n, self.k, self.group_size,
+                           self.dtype)
 
 
 # ------------------------------------------------------------ CPU packer
@@ -183,20 +189,19 @@ def prepare_w4a16(p, dtype=torch.bfloat16):
     _validate(p)
     if dtype not in (torch.float16, torch.bfloat16):
         raise TypeError("W4A16 weights pair with fp16 or bf16 activations")
-    words = p.data if p.layout == "nk" else p.data.T.contiguous()
-    if p.order == "high":  # reverse the nibble order inside each word
-        w64 = words.to(torch.int64) & 0xFFFFFFFF
-        rev = torch.zeros_like(w64)
-        for j in range(8):
-            rev |= ((w64 >> (4 * j)) & 15) << (28 - 4 * j)
-        words = rev.to(torch.int32)
-    words = words.contiguous()
-    flipped = torch.empty_like(words)
-    nat.check(nat.library().b2_int4_to_w4a16_words(words.data_ptr(), flipped.data_ptr(), words.numel(),
-                                                   nat.stream_ptr(words.device)), "b2_int4_to_w4a16_words")
-    zu = (p.zeros + 8).to(dtype)            # integers 0..15, exact in 16 bits
-    return W4A16Weight(flipped, p.scales.to(dtype).contiguous(), zu.contiguous(), p.n, p.k,
-                       p.group_size, dtype)
+    if p.k % 64:
+        raise ValueError("W4A16 kernel needs K divisible by 64")
+    lib = nat.library()
+    t = -(-p.n // 128)
+    tiles = torch.empty((t, p.k // 64, 128, 8), device=p.data.device, dtype=torch.int32)
+    groups = torch.empty((t, p.k // p.group_size, 128), device=p.data.device, dtype=torch.int32)
+    assert tiles.numel() * 4 == lib.b2_w4a16_tiles_bytes(p.n, p.k)
+    assert groups.numel() * 4 == lib.b2_w4a16_groups_bytes(p.n, p.k, p.group_size)
+    nat.check(lib.b2_w4a16_prepare(
+        p.data.data_ptr(), int(p.layout == "kn"), int(p.order == "high"), p.scales.data_ptr(),
+        p.zeros.data_ptr(), p.n, p.k, p.group_size, nat.DTYPE_CODE[dtype], tiles.data_ptr(),
+        groups.data_ptr(), nat.stream_ptr(p.data.device)), "b2_w4a16_prepare")
+    return W4A16Weight(tiles, groups, p.n, p.k, p.group_size, dtype)
 
 
 def quantize_w4a16(w, *, group_size=128, dtype=torch.bfloat16):
@@ -211,7 +216,7 @@ def w4a16_gemm(a, wt, bias=None, *, workspace=None):
         raise TypeError("W4A16Weight required")
     if a.dtype != wt.dtype or a.ndim != 2 or a.shape[1] != wt.k:
         raise ValueError(f"Matching {wt.dtype} activation [M,{wt.k}] required")
-    dev = nat.require_device(a, wt.words, bias)
+    dev = nat.require_device(a, wt.tiles, bias)
     if a.stride(1) != 1 or (a.shape[0] > 1 and (a.stride(0) * 2) % 16) or a.data_ptr() % 16:
         a = a.contiguous()
     m = a.shape[0]
@@ -219,13 +224,13 @@ def w4a16_gemm(a, wt, bias=None, *, workspace=None):
     lib = nat.library()
     need = lib.b2_w4a16_workspace_bytes(m, wt.n, wt.k, wt.group_size)
     if need and (workspace is None or workspace.numel() < need):
-        workspace = torch.empty(need, device=dev, dtype=torch.uint8)
+        # arrival counters at the end must start at zero; calls keep them zero
+        workspace = torch.zeros(need, device=dev, dtype=torch.uint8)
     nat.check(lib.b2_w4a16_gemm(
-        a.data_ptr(), nat.DTYPE_CODE[a.dtype], a.stride(0) if m > 1 else wt.k, wt.words.data_ptr(),
-        wt.k // 8, wt.scales.data_ptr(), wt.zeros.data_ptr(), wt.k // wt.group_size, wt.group_size,
-        m, wt.n, wt.k, nat.ptr(bias), nat.DTYPE_CODE[bias.dtype] if bias is not None else 0,
-        out.data_ptr(), wt.n, None if not need else workspace.data_ptr(), need, nat.stream_ptr(dev)),
-        "b2_w4a16_gemm")
+        a.data_ptr(), nat.DTYPE_CODE[a.dtype], a.stride(0) if m > 1 else wt.k, wt.tiles.data_ptr(),
+        wt.groups.data_ptr(), wt.group_size, m, wt.n, wt.k, nat.ptr(bias),
+        nat.DTYPE_CODE[bias.dtype] if bias is not None else 0, out.data_ptr(), wt.n,
+        None if not need else workspace.data_ptr(), need, nat.stream_ptr(dev)), "b2_w4a16_gemm")
     return out
 
 

@@ -48,6 +48,52 @@ def test_pack_int4_matches_reference_golden(golden, g, sym, layout, order):
                           z[key + "_float"].view(np.uint32))
 
 
+def _tiles_cpu(p, dtype):
+    """numpy restatement of the W4A16 tile format (include/b2_qlinear.h):
+    u = q + 8 with element j of a word at nibble (j >> 1) + 4*(j & 1), 4 KiB
+    chunks [T][K/64][128][8]; group words {16-bit scale, zu} [T][G][128]."""
+    words = p.data.cpu().numpy().view(np.uint32)
+    if p.layout == "kn":
+        words = words.T
+    words = np.ascontiguousarray(words).astype(np.uint64)
+    shifts = np.arange(8, dtype=np.uint64) * 4
+    if p.order == "high":
+        shifts = 28 - shifts
+    nib = ((words[..., None] >> shifts) & 15) ^ 8                      # [N, K/8, 8] = u
+    pos = np.array([(j >> 1) + 4 * (j & 1) for j in range(8)], dtype=np.uint64) * 4
+    inter = (nib << pos).sum(-1).astype(np.uint32)                      # [N, K/8]
+    t = -(-p.n // 128)
+    pad = np.zeros((t * 128, p.k // 8), np.uint32)
+    pad[:p.n] = inter
+    tiles = pad.reshape(t, 128, p.k // 64, 8).transpose(0, 2, 1, 3)
+    s16 = p.scales.cpu().to(dtype).view(torch.int16).numpy().view(np.uint16).astype(np.uint32)
+    z16 = (p.zeros.cpu() + 8).to(dtype).view(torch.int16).numpy().view(np.uint16).astype(np.uint32)
+    g = p.k // p.group_size
+    grp = np.zeros((t * 128, g), np.uint32)
+    grp[:p.n] = s16 | (z16 << 16)
+    return np.ascontiguousarray(tiles), np.ascontiguousarray(grp.reshape(t, 128, g).transpose(0, 2, 1))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("g", [32, 64, 128])
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+@pytest.mark.parametrize("order", ["low", "high"])
+def test_prepare_w4a16_tiles_bit_exact(golden, dtype, g, layout, order):
+    """b2_w4a16_prepare == the numpy restatement, from the reference's golden
+    packs of every layout / nibble order (zero rows and full nibble ranges)."""
+    z = golden("int4_packing.npz")
+    key = f"g{g}_aff_{layout}_{order}"
+    n, k = z["w"].shape
+    if k % 64:
+        pytest.skip("W4A16 tiles need K % 64 == 0")
+    p = i4.PackedInt4(*(torch.from_numpy(z[key + "_" + f]) for f in ("data", "scales", "zeros", "sums")),
+                      n, k, g, False, layout, order)
+    wt = i4.prepare_w4a16(p.to("cuda"), dtype)
+    tiles, grp = _tiles_cpu(p, dtype)
+    assert np.array_equal(wt.tiles.cpu().numpy().view(np.uint32), tiles)
+    assert np.array_equal(wt.groups.cpu().numpy().view(np.uint32), grp)
+
+
 def _ref_w4a16(a_bits, a_code, p_cpu, dtype):
     """fp64 oracle: bf16/fp16-rounded scales, w = round((u - zu) * s), fp64 dot."""
     s16 = p_cpu.scales.to(dtype).float().numpy()
@@ -86,6 +132,24 @@ def test_w4a16_small_shapes(dtype, m, n, k, g):
     _check(y, ref, absref, dtype, bias)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("m", [1, 5, 16, 17, 40, 64, 100, 128, 129, 300])
+@pytest.mark.parametrize("g", [32, 128])
+def test_w4a16_schedules(dtype, m, g):
+    """Stream-K (M <= 128: a CTA's range crosses tiles, group stages start
+    mid-group) and whole-tile (M > 128, ragged token and row tiles) runs
+    against the oracle; N = 1000 leaves a partial last row tile."""
+    n, k = 1000, 1152
+    gen = torch.Generator().manual_seed(20261108 + m + g)
+    w = torch.randn((n, k), generator=gen) * 0.05
+    p_cpu = i4.pack_int4_cpu(w, group_size=g, symmetric=False)
+    a = torch.randn((m, k), generator=gen).to(dtype)
+    bias = (torch.randn(n, generator=gen) * 0.1).to(dtype)
+    y = i4.int4_linear_a16(a.cuda(), p_cpu.to("cuda"), bias=bias.cuda())
+    ref, absref = _ref_w4a16(_bits(a), ODT[dtype], p_cpu, dtype)
+    _check(y, ref, absref, dtype, bias)
+
+
 @pytest.mark.parametrize("m", [1, 16, 128, 2048])
 def test_w4a16_config3(m):
     """bf16 A [M,4096], W [14336,4096] N(0,0.02) affine uint4
@@ -112,7 +176,7 @@ def test_w4a16_deterministic_split_k():
     w = torch.randn((4096, 4096), generator=gen, device="cuda") * 0.02
     wt = i4.quantize_w4a16(w, group_size=128, dtype=dtype)
     a = torch.randn((8, 4096), generator=gen, device="cuda").to(dtype)
-    assert nat.library().b2_w4a16_workspace_bytes(8, 4096, 4096, 128) > 0  # split-K engaged
+    assert nat.library().b2_w4a16_workspace_bytes(8, 4096, 4096, 128) > 0  # stream-K slots engaged
     y1, y2 = i4.w4a16_gemm(a, wt), i4.w4a16_gemm(a, wt)
     assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
 
@@ -126,3 +190,23 @@ def test_dense_linear_kind_f16(dtype):
     y = i4.dense_linear(a.cuda(), w.cuda())
     af, wf = oracle.decode(_bits(a), ODT[dtype]), oracle.decode(_bits(w), ODT[dtype])
     _check(y, oracle.gemm_f32_f64(af, wf), oracle.gemm_f32_f64(np.abs(af), np.abs(wf)), dtype)
+
+
+def test_w4a16_workspace_reuse_leaves_counters_zero():
+    """One caller-owned workspace across decode calls of different shapes:
+    results equal fresh-workspace calls bit for bit, and the arrival
+    counters at its end are zero again after every call."""
+    dtype = torch.bfloat16
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    shapes = [(8, 4096, 2048), (1, 1000, 1152), (32, 2304, 4096), (8, 4096, 2048)]
+    lib = nat.library()
+    need = max(lib.b2_w4a16_workspace_bytes(m, n, k, 128) for m, n, k in shapes)
+    ws = torch.zeros(need, device="cuda", dtype=torch.uint8)
+    for m, n, k in shapes:
+        w = torch.randn((n, k), generator=gen, device="cuda") * 0.02
+        wt = i4.quantize_w4a16(w, group_size=128, dtype=dtype)
+        a = torch.randn((m, k), generator=gen, device="cuda").to(dtype)
+        y_shared = i4.w4a16_gemm(a, wt, workspace=ws)
+        y_fresh = i4.w4a16_gemm(a, wt)
+        assert torch.equal(y_shared.view(torch.int16), y_fresh.view(torch.int16))
+        assert int(ws[:4096].count_nonzero()) == 0  # the arrival counters
