@@ -303,6 +303,30 @@ __device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
         "+r"(r[31])::"memory");
 }
 
+// One lane of a converged warp (the lowest active lane, the same lane on
+// every call from the same converged warp).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\telect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// AND of `v` over the `n` threads meeting at named barrier `id`: every
+// participant leaves with the same answer (a uniform abort decision).
+__device__ __forceinline__ bool bar_and(int id, int n, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

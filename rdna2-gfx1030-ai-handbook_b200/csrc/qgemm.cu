@@ -303,72 +303,78 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status)) {
-            ok = false;
-            break;
-          }
+    // Producer.  The whole warp runs the loop and one elected lane issues:
+    // a loop run by a single lane of a diverged warp pays a large
+    // per-iteration cost on this part.
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status));
+        if (!ok) break;
+        if (elect_one()) {
           mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
-          tma_load_2d(&tma_a, &full[stage], smem + L::kOffA + stage * L::kABytes, kb * kKbElems,
-                      tm * 128);
-          tma_load_2d(&tma_b, &full[stage], smem + L::kOffB + stage * L::kBBytes, kb * kKbElems,
-                      tn * BN);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          tma_load_2d(&tma_a, &full[stage], smem + L::kOffA + stage * L::kABytes, kb * kKbElems, tm * 128);
+          tma_load_2d(&tma_b, &full[stage], smem + L::kOffB + stage * L::kBBytes, kb * kKbElems, tn * BN);
         }
-      }
-      // Tail: wait until the MMA warp has released every slot, so no commit
-      // is still in flight to this CTA's barriers when it exits.
-      for (int i = 0; i < STAGES && ok; ++i) {
-        ok = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status);
+        __syncwarp();
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
         }
       }
     }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc<KIND>(128, BN);
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      int t = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
-        const int buf = t & 1;
-        const uint32_t use = static_cast<uint32_t>(t >> 1);
-        if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag, kSiteMmaTmem, p.status)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteMma, p.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + L::kOffA + stage * L::kABytes);
-          const uint32_t b_addr = smem_u32(smem + L::kOffB + stage * L::kBBytes);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma<KIND>(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32), idesc,
-                       (kb | kk) != 0 ? 1u : 0u);
-          umma_commit(&empty[stage]);
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
-        }
-        if (!ok) break;
-        umma_commit(&tfull[buf]);
+    // Tail: wait until the MMA warp has released every slot, so no commit
+    // is still in flight to this CTA's barriers when it exits.
+    for (int i = 0; i < STAGES && ok; ++i) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status));
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
       }
+    }
+  } else if (warp == 1) {
+    // MMA issuer: whole warp loops, one elected lane (the same lane every
+    // time, so its commits cover its own MMAs) issues.  Descriptors are
+    // built once; stepping stages and K slices adds to the address field.
+    constexpr uint32_t idesc = make_idesc<KIND>(128, BN);
+    const uint64_t a_desc0 = sw128_desc(smem_u32(smem + L::kOffA));
+    const uint64_t b_desc0 = sw128_desc(smem_u32(smem + L::kOffB));
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
+      const int buf = t & 1;
+      const uint32_t use = static_cast<uint32_t>(t >> 1);
+      ok = __all_sync(0xffffffffu, mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag, kSiteMmaTmem, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag, kSiteMma, p.status));
+        if (!ok) break;
+        tc_fence_after();
+        if (elect_one()) {
+          const uint64_t ad = a_desc0 + static_cast<uint32_t>((stage * L::kABytes) >> 4);
+          const uint64_t bd = b_desc0 + static_cast<uint32_t>((stage * L::kBBytes) >> 4);
+          umma<KIND>(d_tmem, ad, bd, idesc, kb != 0 ? 1u : 0u);
+          umma<KIND>(d_tmem, ad + 2, bd + 2, idesc, 1u);
+          umma<KIND>(d_tmem, ad + 4, bd + 4, idesc, 1u);
+          umma<KIND>(d_tmem, ad + 6, bd + 6, idesc, 1u);
+          umma_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) break;
+      if (elect_one()) umma_commit(&tfull[buf]);
+      __syncwarp();
     }
   } else {
     const int quarter = warp & 3;  // TMEM lanes this warp may access
@@ -459,42 +465,46 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0) {
-      const uint32_t full_leader = mapa_shared(smem_u32(&full[0]), 0);
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status)) {
-            ok = false;
-            break;
-          }
+    // Producer (whole warp loops, one elected lane issues).
+    const uint32_t full_leader = mapa_shared(smem_u32(&full[0]), 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      const int tm = tile % p.tiles_m, tn = tile / p.tiles_m;
+      for (int kb = 0; kb < p.num_kb; ++kb) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status));
+        if (!ok) break;
+        if (elect_one()) {
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
           const uint32_t fb = full_leader + static_cast<uint32_t>(stage * 8);
           tma_load_2d_pair(&tma_a, fb, smem + L::kOffA + stage * L::kABytes, kb * kKbElems,
                            tm * 256 + static_cast<int>(rank) * 128);
           tma_load_2d_pair(&tma_b, fb, smem + L::kOffB + stage * L::kBBytes, kb * kKbElems,
                            tn * BN + static_cast<int>(rank) * (BN / 2));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
         }
-      }
-      // Tail: every slot released (and forwarded) before exit.
-      for (int i = 0; i < STAGES && ok; ++i) {
-        ok = mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status);
+        __syncwarp();
         if (++stage == STAGES) {
           stage = 0;
           phase ^= 1u;
         }
       }
     }
+    // Tail: every slot released before exit.
+    for (int i = 0; i < STAGES && ok; ++i) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status));
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
   } else if (warp == 1) {
-    if (leader && lane == 0) {
+    if (leader) {
+      // MMA issuer of the pair (leader CTA): whole warp loops, one elected
+      // lane issues; descriptors built once, stages stepped by adds.
       constexpr uint32_t idesc = make_idesc<KIND>(256, BN);
+      const uint64_t a_desc0 = sw128_desc(smem_u32(smem + L::kOffA));
+      const uint64_t b_desc0 = sw128_desc(smem_u32(smem + L::kOffB));
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -502,31 +512,34 @@ __global__ void __launch_bounds__(192, 1)
       for (int tile = pair; tile < num_tiles && ok; tile += npairs, ++t) {
         const int buf = t & 1;
         const uint32_t use = static_cast<uint32_t>(t >> 1);
-        if (!mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag, kSiteMmaTmem, p.status)) break;
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(&tempty[buf], (use & 1u) ^ 1u, abort_flag, kSiteMmaTmem, p.status));
+        if (!ok) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, kSiteMma, p.status)) {
-            ok = false;
-            break;
+          ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag, kSiteMma, p.status));
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
+            const uint64_t ad = a_desc0 + static_cast<uint32_t>((stage * L::kABytes) >> 4);
+            const uint64_t bd = b_desc0 + static_cast<uint32_t>((stage * L::kBBytes) >> 4);
+            umma_pair<KIND>(d_tmem, ad, bd, idesc, kb != 0 ? 1u : 0u);
+            umma_pair<KIND>(d_tmem, ad + 2, bd + 2, idesc, 1u);
+            umma_pair<KIND>(d_tmem, ad + 4, bd + 4, idesc, 1u);
+            umma_pair<KIND>(d_tmem, ad + 6, bd + 6, idesc, 1u);
+            // One completion signal to both CTAs' `empty[stage]` barriers.
+            umma_commit_pair_both(smem_u32(&empty[stage]));
           }
-          const uint32_t a_addr = smem_u32(smem + L::kOffA + stage * L::kABytes);
-          const uint32_t b_addr = smem_u32(smem + L::kOffB + stage * L::kBBytes);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            umma_pair<KIND>(d_tmem, sw128_desc(a_addr + kk * 32), sw128_desc(b_addr + kk * 32),
-                            idesc, (kb | kk) != 0 ? 1u : 0u);
-          // One completion signal to both CTAs' `empty[stage]` barriers.
-          umma_commit_pair_both(smem_u32(&empty[stage]));
+          __syncwarp();
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
-          // Peek at the next stage so its wait overlaps the MMAs just issued.
-          if (kb + 1 < p.num_kb) mbar_try_wait(&full[stage], phase);
         }
         if (!ok) break;
-        umma_commit_pair_both(smem_u32(&tfull[buf]));
+        if (elect_one()) umma_commit_pair_both(smem_u32(&tfull[buf]));
+        __syncwarp();
       }
     }
   } else {

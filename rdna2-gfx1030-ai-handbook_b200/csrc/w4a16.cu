@@ -133,30 +133,6 @@ __device__ __forceinline__ void sts_v4(uint32_t addr, uint4 v) {
                : "memory");
 }
 
-// One lane of a converged warp (the lowest active lane, the same lane on
-// every call from the same converged warp).
-__device__ __forceinline__ bool elect_one() {
-  uint32_t pred;
-  asm volatile(
-      "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\telect.sync r|p, 0xffffffff;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(pred));
-  return pred != 0;
-}
-
-// AND of `v` over the `n` threads meeting at named barrier `id`: every
-// participant leaves with the same answer (a uniform abort decision).
-__device__ __forceinline__ bool bar_and(int id, int n, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
-      "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(v)), "r"(id), "r"(n)
-      : "memory");
-  return r != 0;
-}
-
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
@@ -434,7 +410,11 @@ __global__ void __launch_bounds__(w4_threads<BT, RK, RS, XS, UK>(), 1)
     // elements).  XS units are in flight at once.
     const int t = threadIdx.x - 64;
     const int gi = t / (128 * UK), sub = (t / 128) % UK, r = t & 127;
-    const int ha = (r >> 2) & 1;  // lane-staggered half order: conflict-free 16-byte loads
+    // Natural half order: each 16-byte store of a quarter-warp (8 rows)
+    // lands on 8 distinct chunk columns of the 128B swizzle (conflict-free);
+    // the two 16-byte loads of the packed words are 2-way conflicted instead,
+    // the cheaper side of the trade (2 loads against 8 stores per k-block).
+    constexpr int ha = 0;
     // Row r of k-block `sub` of slot gi, 128B swizzle: 16-byte chunk c lives
     // at chunk c ^ (r & 7).
     const uint32_t xrow =
@@ -558,12 +538,13 @@ __device__ __forceinline__ bool wait_count(const int* ctr, int target, volatile 
 }
 
 // ------------------------------------------------------------------ decode
-// Decode kernel (M <= 32, stream-K): no MMA warp and no per-k-block hand-off
-// between warps.  NG transform groups of 4 warps; group g dequantizes the
-// k-blocks i = g, g + NG, ... of this CTA's k-block sequence into its two
-// ping-pong slots and, after a group barrier, one elected lane of the group
-// issues that k-block's 4 MMAs into the group's own TMEM accumulator.  The
-// epilogue sums a segment's NG accumulators in group order (deterministic).
+// Decode kernel (M <= 32, stream-K).  NG groups, each of 4 transform warps
+// and its own MMA warp: group g owns the k-blocks i = g, g + NG, ... of this
+// CTA's k-block sequence, dequantizes them into its two ping-pong slots and
+// accumulates them into its own TMEM accumulator, so a group's MMA warp
+// handles only every NG-th k-block and no transform warp ever waits on MMA
+// issue.  The epilogue sums a segment's NG accumulators in group order
+// (deterministic).
 template <int BT, int RK, int RS, int NG>
 struct W4DecLayout {
   static constexpr int kXf = kW4Rows * 128;            // one k-block slot, SW128
@@ -575,13 +556,18 @@ struct W4DecLayout {
   static constexpr int kOffWords = kOffAct + RS * RK * kAct;
   static constexpr int kOffGrp = kOffWords + RS * kWords;
   static constexpr int kOffBar = kOffGrp + RS * kGrp;
-  static constexpr int kNumBars = 2 * RS + 2 * NG + 5;
+  static constexpr int kNumBars = 2 * RS + 4 * NG + 5;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
   // misc: [0] TMEM base, [4] abort flag
   static constexpr int kAlloc = kOffMisc + 16 + 1024;
   static constexpr uint32_t kCols = 2 * NG * BT;       // [buffer][group] accumulators
   static constexpr uint32_t kTmemCols = kCols <= 32 ? 32 : kCols <= 64 ? 64 : kCols <= 128 ? 128 : kCols <= 256 ? 256 : 512;
-  static constexpr int kThreads = 64 + NG * 128 + 128;
+  // warps: producer, NG MMA warps (the first also owns TMEM), NG groups of 4
+  // transform warps, 4 epilogue warps
+  static constexpr int kMmaWarp0 = 1;
+  static constexpr int kXfWarp0 = 1 + NG;
+  static constexpr int kEpiWarp0 = kXfWarp0 + 4 * NG;
+  static constexpr int kThreads = 32 * (kEpiWarp0 + 4);
   static_assert(kAlloc <= 232448, "shared memory budget");
   static_assert(kCols <= 512, "TMEM budget");
   static_assert(BT <= 32, "decode token tiles");
@@ -596,23 +582,27 @@ __global__ void __launch_bounds__(W4DecLayout<BT, RK, RS, NG>::kThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint64_t* full_raw = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
   uint64_t* raw_empty = full_raw + RS;
-  uint64_t* slot_empty = raw_empty + RS;  // [NG][2]
+  uint64_t* slot_full = raw_empty + RS;    // [NG][2]
+  uint64_t* slot_empty = slot_full + 2 * NG;  // [NG][2]
   uint64_t* acc_full = slot_empty + 2 * NG;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int kEpiWarp0 = 2 + 4 * NG;
+  constexpr int kEpiWarp0 = L::kEpiWarp0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < RS; ++s) {
       mbar_init(&full_raw[s], 1);
-      mbar_init(&raw_empty[s], 4 * NG + NG);  // every transform warp + one commit per group
+      mbar_init(&raw_empty[s], 4 * NG + NG);  // every transform warp + each MMA warp's commit
     }
-    for (int s = 0; s < 2 * NG; ++s) mbar_init(&slot_empty[s], 1);
+    for (int s = 0; s < 2 * NG; ++s) {
+      mbar_init(&slot_full[s], 4);   // the group's transform warps
+      mbar_init(&slot_empty[s], 1);  // the group's MMA commit
+    }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&acc_full[b], NG);  // one commit per group
+      mbar_init(&acc_full[b], NG);  // one commit per MMA warp
       mbar_init(&acc_empty[b], 4);
     }
     mbar_init(drain, NG);
@@ -620,7 +610,7 @@ __global__ void __launch_bounds__(W4DecLayout<BT, RK, RS, NG>::kThreads, 1)
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) tma_prefetch_desc(&tma_a);
-  if (warp == 1) {
+  if (warp == L::kMmaWarp0) {
     tmem_alloc(tmem_slot, L::kTmemCols);
     tmem_relinquish();
   }
@@ -676,46 +666,90 @@ __global__ void __launch_bounds__(W4DecLayout<BT, RK, RS, NG>::kThreads, 1)
           while (!mbar_try_wait(&full_raw[i], (live_par >> i) & 1u) && globaltimer() - t0 < kWaitLimitNs) {
           }
     }
-  } else if (warp == 1) {
-    // ---- TMEM owner: before release, wait until every group's MMAs are done.
-    if (lane == 0) {
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitLimitNs) {
-      }
-    }
-    __syncwarp();
-  } else if (warp < kEpiWarp0) {
-    // ---- transform + MMA issue, group g of 4 warps; thread = weight row r.
-    const int t = threadIdx.x - 64;
-    const int g = t >> 7, r = t & 127, gw = (t >> 5) & 3;
-    const int gbar = 2 + g;  // this group's named barrier
-    const int ha = (r >> 2) & 1;
-    // Slot 1 sits kXf bytes after slot 0: its addresses are slot 0's + kXf
-    // (and + kXf >> 4 in a descriptor's address field).
-    const uint32_t base0 = smem_u32(smem + L::kOffXf + 2 * g * L::kXf);
-    const uint32_t xrow0 = (base0 + r * 128) | ((r & 7) << 4);
-    const uint32_t xa0 = xrow0 ^ ((4 * ha) << 4), xb0 = xrow0 ^ ((4 * (ha ^ 1)) << 4);
-    const uint64_t a_desc0 = sw128_desc(base0);
-    const uint64_t b_desc0 = sw128_desc(smem_u32(smem + L::kOffAct));
+  } else if (warp < L::kXfWarp0) {
+    // ---- MMA warp of group g: the k-blocks i = g, g + NG, ... of this CTA's
+    // sequence, into the group's own accumulator.  Whole warp loops, one
+    // elected lane (always the same) issues and commits.
+    const int g = warp - L::kMmaWarp0;
     constexpr uint32_t idesc = (1u << 4) | (BF16 ? (1u << 7) | (1u << 10) : 0u) |
                                (static_cast<uint32_t>(BT >> 3) << 17) |
                                (static_cast<uint32_t>(kW4Rows >> 4) << 24);
+    const uint64_t a_desc0 = sw128_desc(smem_u32(smem + L::kOffXf + 2 * g * L::kXf));
+    const uint64_t b_desc0 = sw128_desc(smem_u32(smem + L::kOffAct));
     int rs = 0, i = 0, jg = 0, seg_i = 0;
-    uint32_t rph = 0;
     bool ok = true;
     int64_t cur = w4_first(p);
     W4Seg s;
     while (ok && w4_next(p, cur, s)) {
       const int b = seg_i & 1;
       const uint32_t d = tmem_base + static_cast<uint32_t>((b * NG + g) * BT);
-      // The accumulator buffer is free once the epilogue drained it.
-      ok = bar_and(gbar, 128, mbar_wait(&acc_empty[b], ((seg_i >> 1) & 1) ^ 1u, abort_flag, kSiteMmaTmem, p.status));
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&acc_empty[b], ((seg_i >> 1) & 1) ^ 1u, abort_flag, kSiteMmaTmem, p.status));
       if (!ok) break;
+      tc_fence_after();
       uint32_t acc = 0;
+      for (int kb = s.kb0; kb < s.kb1 && ok; kb += RK) {
+        const int n = s.kb1 - kb < RK ? s.kb1 - kb : RK;
+        for (int j = 0; j < n; ++j, ++i) {
+          if (i % NG != g) continue;
+          const int sl = jg & 1;
+          ok = __all_sync(0xffffffffu, mbar_wait(&slot_full[2 * g + sl], (jg >> 1) & 1, abort_flag, kSiteMma, p.status));
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
+            const uint64_t ad = a_desc0 + static_cast<uint32_t>((sl * L::kXf) >> 4);
+            const uint64_t bd = b_desc0 + static_cast<uint32_t>(((rs * RK + j) * L::kAct) >> 4);
+            umma<kKindBF16>(d, ad, bd, idesc, acc);
+            umma<kKindBF16>(d, ad + 2, bd + 2, idesc, 1u);
+            umma<kKindBF16>(d, ad + 4, bd + 4, idesc, 1u);
+            umma<kKindBF16>(d, ad + 6, bd + 6, idesc, 1u);
+            umma_commit(&slot_empty[2 * g + sl]);
+          }
+          __syncwarp();
+          acc = 1;
+          ++jg;
+        }
+        if (!ok) break;
+        // the stage's activation tiles are free once this warp's MMAs are done
+        if (elect_one()) umma_commit(&raw_empty[rs]);
+        __syncwarp();
+        if (++rs == RS) rs = 0;
+      }
+      if (!ok) break;
+      if (elect_one()) umma_commit(&acc_full[b]);
+      __syncwarp();
+      ++seg_i;
+    }
+    // Before TMEM is released: every MMA of every group complete.
+    if (elect_one()) umma_commit(drain);
+    __syncwarp();
+    if (g == 0 && lane == 0) {
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitLimitNs) {
+      }
+    }
+    __syncwarp();
+  } else if (warp < kEpiWarp0) {
+    // ---- transform, group g of 4 warps; thread = weight row r.  Each warp
+    // runs on its own (no group barrier): it arrives on the slot's full
+    // barrier after its rows are written.
+    const int t = threadIdx.x - 32 * L::kXfWarp0;
+    const int g = t >> 7, r = t & 127;
+    constexpr int ha = 0;  // natural half order (conflict-free 16-byte stores)
+    // Slot 1 sits kXf bytes after slot 0: its addresses are slot 0's + kXf.
+    const uint32_t base0 = smem_u32(smem + L::kOffXf + 2 * g * L::kXf);
+    const uint32_t xrow0 = (base0 + r * 128) | ((r & 7) << 4);
+    const uint32_t xa0 = xrow0 ^ ((4 * ha) << 4), xb0 = xrow0 ^ ((4 * (ha ^ 1)) << 4);
+    int rs = 0, i = 0, jg = 0;
+    uint32_t rph = 0;
+    bool ok = true;
+    int64_t cur = w4_first(p);
+    W4Seg s;
+    while (ok && w4_next(p, cur, s)) {
       for (int kb = s.kb0; kb < s.kb1; kb += RK) {
         const int n = s.kb1 - kb < RK ? s.kb1 - kb : RK;
         const int g_lo = (kb * 64) >> p.gshift;
-        ok = bar_and(gbar, 128, mbar_wait(&full_raw[rs], rph, abort_flag, kSiteTransform, p.status));
+        ok = __all_sync(0xffffffffu, mbar_wait(&full_raw[rs], rph, abort_flag, kSiteTransform, p.status));
         if (!ok) break;
         const uint32_t words = smem_u32(smem + L::kOffWords + rs * L::kWords) + r * 32;
         const uint32_t grp = smem_u32(smem + L::kOffGrp + rs * L::kGrp) + r * 4;
@@ -723,69 +757,37 @@ __global__ void __launch_bounds__(W4DecLayout<BT, RK, RS, NG>::kThreads, 1)
           if (i % NG != g) continue;
           const int sl = jg & 1;
           const uint32_t xa = xa0 + sl * L::kXf, xb = xb0 + sl * L::kXf;
-          const bool free = mbar_wait(&slot_empty[2 * g + sl], ((jg >> 1) & 1) ^ 1u, abort_flag, kSiteTransform,
-                                      p.status);
-          if (free) {
-            const uint4 wa = lds_v4(words + j * kW4Chunk + ha * 16);
-            const uint4 wb = lds_v4(words + j * kW4Chunk + (ha ^ 1) * 16);
-            const int ga = (((kb + j) * 64 + ha * 32) >> p.gshift) - g_lo;
-            const int gb = (((kb + j) * 64 + (ha ^ 1) * 32) >> p.gshift) - g_lo;
-            uint32_t za, sa, zb, sb;
-            group_operands<BF16>(lds_u32(grp + ga * kW4Rows * 4), za, sa);
-            group_operands<BF16>(lds_u32(grp + gb * kW4Rows * 4), zb, sb);
-            sts_v4(xa ^ (0 << 4), dequant_word<BF16>(wa.x, za, sa));
-            sts_v4(xa ^ (1 << 4), dequant_word<BF16>(wa.y, za, sa));
-            sts_v4(xa ^ (2 << 4), dequant_word<BF16>(wa.z, za, sa));
-            sts_v4(xa ^ (3 << 4), dequant_word<BF16>(wa.w, za, sa));
-            sts_v4(xb ^ (0 << 4), dequant_word<BF16>(wb.x, zb, sb));
-            sts_v4(xb ^ (1 << 4), dequant_word<BF16>(wb.y, zb, sb));
-            sts_v4(xb ^ (2 << 4), dequant_word<BF16>(wb.z, zb, sb));
-            sts_v4(xb ^ (3 << 4), dequant_word<BF16>(wb.w, zb, sb));
-            fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
-          }
-          // Group barrier: the slot is complete (and the group agrees on aborts).
-          ok = bar_and(gbar, 128, free);
+          ok = __all_sync(0xffffffffu, mbar_wait(&slot_empty[2 * g + sl], ((jg >> 1) & 1) ^ 1u, abort_flag,
+                                                 kSiteTransform, p.status));
           if (!ok) break;
-          if (gw == 0) {
-            tc_fence_after();
-            if (elect_one()) {
-              const uint64_t ad = a_desc0 + static_cast<uint32_t>((sl * L::kXf) >> 4);
-              const uint64_t bd = b_desc0 + static_cast<uint32_t>(((rs * RK + j) * L::kAct) >> 4);
-              umma<kKindBF16>(d, ad, bd, idesc, acc);
-              umma<kKindBF16>(d, ad + 2, bd + 2, idesc, 1u);
-              umma<kKindBF16>(d, ad + 4, bd + 4, idesc, 1u);
-              umma<kKindBF16>(d, ad + 6, bd + 6, idesc, 1u);
-              umma_commit(&slot_empty[2 * g + sl]);
-            }
-            __syncwarp();
-          }
-          acc = 1;
+          const uint4 wa = lds_v4(words + j * kW4Chunk + ha * 16);
+          const uint4 wb = lds_v4(words + j * kW4Chunk + (ha ^ 1) * 16);
+          const int ga = (((kb + j) * 64 + ha * 32) >> p.gshift) - g_lo;
+          const int gb = (((kb + j) * 64 + (ha ^ 1) * 32) >> p.gshift) - g_lo;
+          uint32_t za, sa, zb, sb;
+          group_operands<BF16>(lds_u32(grp + ga * kW4Rows * 4), za, sa);
+          group_operands<BF16>(lds_u32(grp + gb * kW4Rows * 4), zb, sb);
+          sts_v4(xa ^ (0 << 4), dequant_word<BF16>(wa.x, za, sa));
+          sts_v4(xa ^ (1 << 4), dequant_word<BF16>(wa.y, za, sa));
+          sts_v4(xa ^ (2 << 4), dequant_word<BF16>(wa.z, za, sa));
+          sts_v4(xa ^ (3 << 4), dequant_word<BF16>(wa.w, za, sa));
+          sts_v4(xb ^ (0 << 4), dequant_word<BF16>(wb.x, zb, sb));
+          sts_v4(xb ^ (1 << 4), dequant_word<BF16>(wb.y, zb, sb));
+          sts_v4(xb ^ (2 << 4), dequant_word<BF16>(wb.z, zb, sb));
+          sts_v4(xb ^ (3 << 4), dequant_word<BF16>(wb.w, zb, sb));
+          fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&slot_full[2 * g + sl]);
           ++jg;
         }
         if (!ok) break;
-        // Stage done: this warp's reads are over; the group's MMAs that read
-        // the stage's activation tiles are covered by the commit.
         __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);
-        if (gw == 0) {
-          if (elect_one()) umma_commit(&raw_empty[rs]);
-          __syncwarp();
-        }
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);  // this warp's reads of the stage are over
         if (++rs == RS) {
           rs = 0;
           rph ^= 1u;
         }
       }
-      if (!ok) break;
-      if (gw == 0) {
-        if (elect_one()) umma_commit(&acc_full[b]);
-        __syncwarp();
-      }
-      ++seg_i;
-    }
-    if (gw == 0) {  // the TMEM owner waits for this before releasing TMEM
-      if (elect_one()) umma_commit(drain);
-      __syncwarp();
     }
   } else {
     // ---- epilogue: TMEM lane = weight row, column = token; sums the NG
@@ -889,7 +891,7 @@ __global__ void __launch_bounds__(W4DecLayout<BT, RK, RS, NG>::kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == L::kMmaWarp0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, L::kTmemCols);
   }
