@@ -136,6 +136,25 @@ def test_act_quant_bit_exact(dtype, k, block):
     assert np.array_equal(q.cpu().numpy(), ref_q)
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_act_quant_exact_ties_round_to_even(dtype):
+    """Rows whose scale is exactly 1 (absmax 127) with values on x.5: the
+    fast quantizer must defer to the exact division and round ties to even,
+    like the oracle (k = 1024 runs the wide-lane kernel)."""
+    k = 1024
+    x32 = np.zeros((4, k), dtype=np.float32)
+    ties = np.array([0.5, 1.5, 2.5, 3.5, -0.5, -1.5, -2.5, 126.5, -126.5, 64.5], dtype=np.float32)
+    for r in range(4):
+        x32[r, 0] = 127.0
+        x32[r, 1:1 + ties.size] = ties * (1 if r % 2 == 0 else -1)
+    xt = x_tensor(x32, dtype)
+    q, s = rdna2_ops.act_quant(xt, rotation_block=None)
+    ref_q, ref_s = oracle.act_quant_int8(x_bits(xt), ODT[dtype], 0)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), ref_s.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), ref_q)
+    assert list(q.cpu().numpy()[0, 1:5]) == [0, 2, 2, 4]
+
+
 def test_act_quant_e4m3_bit_exact():
     rng = np.random.default_rng(5)
     x32 = outlier_activations(rng, 33, 5120)
