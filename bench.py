@@ -22,6 +22,7 @@ the same workload.
 """
 import argparse
 import json
+import re
 import os
 import statistics
 import sys
@@ -300,9 +301,10 @@ def run_b200(args, rank, world, local_rank):
     int8_peak = 2.0 * pk["bf16_tflops"]
     achieved = 2.0 * M * N * K / (gemm_ms * 1e-3) / 1e12
     traffic = None
-    prof = ROOT / "profiles" / "qgemm_i8_config2_traffic.json"
+    prof = ROOT / "profiles" / "qgemm_pair_c2.md"
     if prof.exists():
-        traffic = json.loads(prof.read_text()).get("dram_bytes_per_launch")
+        hit = re.search(r"dram_bytes_per_launch \| (\d+)", prof.read_text())
+        traffic = int(hit.group(1)) if hit else None
 
     # ---- end to end through the public API with host buffers
     x_host = xs[0].cpu().pin_memory()
@@ -373,7 +375,7 @@ def run_b200(args, rank, world, local_rank):
                          f"({args.sets * (M * K * 2 + N * K) / 2**20:.0f} MiB > 126 MB L2)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
                      "unit": "TOPS", "frac": round(achieved / int8_peak, 4), "traffic": traffic,
-                     "kernel": "qgemm_kernel<kind::i8,BN=256>",
+                     "kernel": "qgemm_pair_kernel<kind::i8,BN=256> (auto path on C2)",
                      "peak_source": f"2 x bf16_tflops ({pk['source']}): kind::i8 issues at twice "
                                     "the kind::f16 rate",
                      "frac_of_nominal_4500": round(achieved / 4500.0, 4),

@@ -715,8 +715,8 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
 // Co-resident 2-CTA clusters of the pair kernel on the current device (the
 // persistent grid size in pairs), or -1 when cluster launch is unavailable.
 int pair_capacity() {
-  using L = Smem<128, 128, 256, 6>;
-  auto kernel = qgemm_pair_kernel<kKindI8, 256, 6>;
+  using L = Smem<128, 128, 256, 7>;
+  auto kernel = qgemm_pair_kernel<kKindI8, 256, 7>;
   static bool configured[64] = {false};
   static int cap[64] = {0};
   const int dev = current_device();
@@ -771,7 +771,9 @@ static cudaError_t dispatch(int cfg, const void* a, int64_t lda, const void* b, 
   switch (cfg) {
     case 3: return launch_single<KIND, 256, 4>(a, lda, b, ldb, p, max_ctas, stream);
     case 4: return launch_single<KIND, 128, 6>(a, lda, b, ldb, p, max_ctas, stream);
-    case 5: return launch_pair<KIND, 256, 6>(a, lda, b, ldb, p, max_ctas, stream);
+    // 7 stages: the ring covers the ~2k-cycle refill (TMA after the slot's
+    // MMAs complete) at 512 tensor cycles per k-block; 6 left a bubble per wrap.
+    case 5: return launch_pair<KIND, 256, 7>(a, lda, b, ldb, p, max_ctas, stream);
     case 6: return launch_pair<KIND, 192, 7>(a, lda, b, ldb, p, max_ctas, stream);
     default: return cudaErrorInvalidValue;
   }
