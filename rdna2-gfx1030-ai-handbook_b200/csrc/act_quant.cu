@@ -285,166 +285,6 @@ __global__ void __launch_bounds__(128)
   }
 }
 
-// Wide-lane variant for the common case -- 16-bit input, INT8 codes, rotation
-// block up to 1024, K a multiple of 1024.  Lane l of a warp holds elements
-// [seg*1024 + 32l, +32) of its segment (four 16-byte loads), so the
-// butterfly stages h = 1..16 run inside the lane and only h >= 32 cross
-// lanes (two shuffle stages for block 128, four in act_quant_kernel).  The
-// stage order and the single rounding per operation are the same as the
-// oracle's.  The quantizer is branch-free per element; one warp vote sends
-// the rare elements near a rounding boundary to the exact division.
-constexpr int kWideMaxWarpsPerRow = 16;
-
-template <int DT>
-__global__ void __launch_bounds__(512)
-    act_quant_wide_kernel(const void* __restrict__ x, int64_t ldx, int M, int wpr, int block, float inv,
-                          uint8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale) {
-  __shared__ float s_max[2][kWideMaxWarpsPerRow];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rows_per_cta = static_cast<int>(blockDim.x) / (32 * wpr);
-  const int g = warp / wpr, part = warp % wpr;
-  const int64_t row_step = static_cast<int64_t>(gridDim.x) * rows_per_cta;
-  const int64_t col = static_cast<int64_t>(part) * 1024 + lane * 32;
-
-  uint4 raw[4];
-  auto issue = [&](int64_t row) {
-    if (row < M) {
-      const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + row * ldx + col);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) raw[c] = __ldcs(p + c);  // streamed once
-    }
-  };
-
-  int64_t base = static_cast<int64_t>(blockIdx.x) * rows_per_cta;
-  issue(base + g);
-  int parity = 0;
-  for (; base < M; base += row_step) {
-    const int64_t row = base + g;
-    const bool live = row < M;
-    float v[32];
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t w[4] = {raw[c].x, raw[c].y, raw[c].z, raw[c].w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if constexpr (DT == kF16) {
-          const __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
-          v[8 * c + 2 * i] = __low2float(h);
-          v[8 * c + 2 * i + 1] = __high2float(h);
-        } else {
-          const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
-          v[8 * c + 2 * i] = __low2float(h);
-          v[8 * c + 2 * i + 1] = __high2float(h);
-        }
-      }
-    }
-    if (!live) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = 0.0f;
-    }
-    if (base + row_step < M) issue(base + row_step + g);  // next row in flight
-
-    if (block > 1) {
-#pragma unroll
-      for (int h = 1; h < 32; h <<= 1) {
-        if (block > h) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (!(i & h)) {
-              const float a = v[i], b = v[i + h];
-              v[i] = __fadd_rn(a, b);
-              v[i + h] = __fsub_rn(a, b);
-            }
-        }
-      }
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        if (block > 32 * d) {
-          // lower lane: v + o; upper lane: o - v (fma(+-1, v, o) rounds once)
-          const float sgn = (lane & d) ? -1.0f : 1.0f;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
-            v[i] = __fmaf_rn(sgn, v[i], o);
-          }
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], inv);
-    }
-
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-    for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
-    if (wpr > 1) {
-      if (lane == 0) s_max[parity][warp] = amax;
-      __syncthreads();
-      for (int w = 0; w < wpr; ++w) amax = fmaxf(amax, s_max[parity][g * wpr + w]);
-      parity ^= 1;
-    }
-    float sc = __fdiv_rn(amax, 127.0f);
-    if (!(sc > 0.0f)) sc = 1.0f;
-    if (!live) continue;
-    const float rcp = __frcp_rn(sc);
-    const bool fast = sc > 1e-30f && sc < 1e30f;
-
-    // Fast codes: rint(RN(v * rcp)) via the 1.5 * 2^23 rounding constant; an
-    // element within 2^-13 of a half-integer (or any element when the scale
-    // is extreme) takes the exact division below.
-    uint32_t packed[8];
-    bool bad = !fast;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      uint32_t c[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float y = __fmul_rn(v[4 * k + j], rcp);
-        const float m = __fadd_rn(y, 12582912.0f);
-        const float n = __fsub_rn(m, 12582912.0f);
-        bad |= !(fabsf(__fsub_rn(n, y)) < 0.4998779296875f);
-        c[j] = __float_as_uint(m);
-      }
-      packed[k] = __byte_perm(__byte_perm(c[0], c[1], 0x0040), __byte_perm(c[2], c[3], 0x0040), 0x5410);
-    }
-    if (__any_sync(0xffffffffu, bad)) {  // rare: redo this lane's codes with the exact test
-#pragma unroll
-      for (int k = 0; k < 8; ++k)
-        packed[k] = pack4<0>(&v[4 * k], sc, rcp, fast);
-    }
-    uint4* dst = reinterpret_cast<uint4*>(q + row * ldq + col);
-    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-    if (part == 0 && lane == 0) scale[row] = sc;
-  }
-}
-
-template <int DT>
-static cudaError_t launch_wide(int64_t M, cudaStream_t st, const void* x, int64_t ldx, int wpr, int block,
-                               float inv, uint8_t* q, int64_t ldq, float* scale) {
-  auto kernel = act_quant_wide_kernel<DT>;
-  const int rows_per_cta = wpr >= 8 ? 1 : 8 / wpr;
-  const int threads = 32 * wpr * rows_per_cta;
-  static int per_sm[64][kWideMaxWarpsPerRow + 1] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  int n = 2;
-  if (dev < 64) {
-    if (per_sm[dev][wpr] == 0) {
-      int b = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, threads, 0) != cudaSuccess || b <= 0) b = 1;
-      per_sm[dev][wpr] = b;
-    }
-    n = per_sm[dev][wpr];
-  }
-  const int64_t need = (M + rows_per_cta - 1) / rows_per_cta;
-  const int64_t cap = static_cast<int64_t>(device_sm_count()) * n;
-  const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
-  kernel<<<grid, threads, 0, st>>>(x, ldx, static_cast<int>(M), wpr, block, inv, q, ldq, scale);
-  return cudaGetLastError();
-}
-
 template <int DT, int SPW, int QUANT>
 static cudaError_t launch_one(int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K, int wpr,
                               int block, float inv, uint8_t* q, int64_t ldq, float* scale, int vin,
@@ -511,13 +351,6 @@ cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   const float inv = block > 1 ? static_cast<float>(1.0 / sqrt(static_cast<double>(block))) : 1.0f;
   uint8_t* qb = static_cast<uint8_t*>(q);
   const int k = static_cast<int>(K);
-  const bool q16 = reinterpret_cast<uintptr_t>(q) % 16 == 0 && ldq % 16 == 0;
-  if (quant == 0 && (x_dtype == kF16 || x_dtype == kBF16) && vin && q16 && K % 1024 == 0 &&
-      K / 1024 <= kWideMaxWarpsPerRow && block <= 1024) {
-    const int w = static_cast<int>(K / 1024);
-    return x_dtype == kF16 ? launch_wide<kF16>(M, stream, x, ldx, w, block, inv, qb, ldq, scale)
-                           : launch_wide<kBF16>(M, stream, x, ldx, w, block, inv, qb, ldq, scale);
-  }
 #define B2_AQ(DT, Q) return launch_spw<DT, Q>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout)
 #define B2_AQ_DT(Q)                 \
   switch (x_dtype) {                \
