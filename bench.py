@@ -396,6 +396,31 @@ def run_b200(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
+def _raw_linear_step(nat, rdna2_ops, torch, dev, xs, wqs, sw, bias, m, n, k, block, kind, x_dtype, out_dtype,
+                     public):
+    """The C-ABI call the public linear makes (b2_quant_linear), checked bit
+    for bit against the public call once, for graph-replayed timing."""
+    lib = nat.library()
+    sets = len(xs)
+    ws_bytes = lib.b2_quant_linear_workspace_bytes(m, k)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    outs = [torch.empty((m, n), device=dev, dtype=out_dtype) for _ in range(sets)]
+
+    def step(i):
+        j = i % sets
+        nat.check(lib.b2_quant_linear(kind, xs[j].data_ptr(), nat.DTYPE_CODE[x_dtype], m, k, k, block or 0,
+                                      wqs[j].data_ptr(), k, n, sw.data_ptr(), sw.numel(),
+                                      bias.data_ptr() if bias is not None else None,
+                                      nat.DTYPE_CODE[bias.dtype] if bias is not None else 0, nat.EPI_SEPARATE,
+                                      outs[j].data_ptr(), nat.DTYPE_CODE[out_dtype], n, ws.data_ptr(), ws_bytes,
+                                      nat.stream_ptr(dev)), "b2_quant_linear")
+    ref = public(xs[0], wqs[0])
+    step(0)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0].view(torch.int16), ref.view(torch.int16)), "raw C-ABI call differs from public call"
+    return step, True
+
+
 def run_workload(args):
     """Configs 1, 3 and 4 of the benchmark plan on one GPU: one JSON line with
     the same timing discipline (warm-up, CUDA events on the launch stream,
@@ -422,9 +447,9 @@ def run_workload(args):
         wq, sw = qlinear.quantize_weight(w)
         wqs = [wq.clone() for _ in range(sets)]
         bias = (torch.randn(n, generator=gen, device=dev) * 0.02).half()
-        ws = torch.empty(nat.library().b2_quant_linear_workspace_bytes(m, k), device=dev, dtype=torch.uint8)
-        step = lambda i: rdna2_ops.w8a8_linear(xs[i % sets], wqs[i % sets], sw, bias,
-                                               out_dtype=torch.float16, workspace=ws)
+        step, graph_ok = _raw_linear_step(nat, rdna2_ops, torch, dev, xs, wqs, sw, bias, m, n, k, None,
+                                          nat.KIND_I8, torch.float16, torch.float16,
+                                          lambda x, w: rdna2_ops.w8a8_linear(x, w, sw, bias, out_dtype=torch.float16))
         metric, flops, launches = "W8A8 INT8 linear TOPS (config 1)", 2.0 * m * n * k, 2
         bound, peak, unit, traffic = "tensor", 2.0 * pk["bf16_tflops"], "TOPS", None
         dtype = "int8"
@@ -467,9 +492,9 @@ def run_workload(args):
         wq, sw = qlinear.quantize_weight(w, quant="e4m3")
         wqs = [wq.clone() for _ in range(sets)]
         xs = [torch.randn((m, k), generator=gen, device=dev).to(torch.bfloat16) for _ in range(sets)]
-        ws = torch.empty(nat.library().b2_quant_linear_workspace_bytes(m, k), device=dev, dtype=torch.uint8)
-        step = lambda i: rdna2_ops.fp8_linear(xs[i % sets], wqs[i % sets], sw, out_dtype=torch.bfloat16,
-                                              workspace=ws)
+        step, graph_ok = _raw_linear_step(nat, rdna2_ops, torch, dev, xs, wqs, sw, None, m, n, k, None,
+                                          nat.KIND_E4M3, torch.bfloat16, torch.bfloat16,
+                                          lambda x, w: rdna2_ops.fp8_linear(x, w, sw, out_dtype=torch.bfloat16))
         metric, flops, launches = f"FP8 e4m3 linear TFLOPS (config 4, M={m})", 2.0 * m * n * k, 2
         traffic = n * k + n * 4 + m * k * 2 + m * n * 2
         if m == 1:
