@@ -486,6 +486,39 @@ def run_workload(args):
         else:
             bound, peak, unit = "tensor", pk["bf16_tflops"], "TFLOP/s"
         dtype = "bf16"
+    elif name.startswith("w4a8m"):
+        # W4A8 (int4_linear_a8) at the config-3 weight shape: int8 A [M,4096]
+        # with per-row scales, uint4 g128 affine W [14336,4096], fp32 out.
+        m, n, k = int(name[5:]), 14336, 4096
+        w = torch.randn((n, k), generator=gen, device=dev) * 0.02
+        wt = i4.prepare_w4a8(i4.pack_int4(w, group_size=128, symmetric=False))
+        del w
+        wts = [wt] + [i4.W4A8Weight(wt.tiles.clone(), wt.groups.clone(), n, k, 128) for _ in range(sets - 1)]
+        xs = [torch.randint(-128, 128, (m, k), generator=gen, device=dev, dtype=torch.int8) for _ in range(sets)]
+        sa = torch.rand(m, generator=gen, device=dev) * 0.02 + 0.001
+        lib = nat.library()
+        need = lib.b2_w4a8_workspace_bytes(m, k, 128)
+        ws = torch.empty(max(need, 256), device=dev, dtype=torch.uint8)
+        outs = [torch.empty((m, n), device=dev, dtype=torch.float32) for _ in range(sets)]
+        ref_out = i4.int4_linear_a8(xs[0], None, sa, prepared=wts[0])
+
+        def raw_step(i):  # the C-ABI call int4_linear_a8 makes, without its host work
+            j = i % sets
+            nat.check(lib.b2_w4a8_gemm(xs[j].data_ptr(), k, wts[j].tiles.data_ptr(), wts[j].groups.data_ptr(), 128,
+                                       m, n, k, sa.data_ptr(), None, 0, 0, outs[j].data_ptr(), n, ws.data_ptr(),
+                                       ws.numel(), nat.stream_ptr(dev)), "b2_w4a8_gemm")
+        raw_step(0)
+        torch.cuda.synchronize()
+        assert torch.equal(outs[0].view(torch.int32), ref_out.view(torch.int32))
+        step, graph_ok = raw_step, True
+        metric, flops = f"W4A8 GEMM TOPS (config-3 shape, M={m})", 2.0 * m * n * k
+        launches = 2
+        traffic = n * k // 2 + n * (k // 128) * 8 + m * k + m * n * 4
+        if m <= 128:
+            bound, peak, unit = "hbm", pk["hbm_gbs"], "GB/s"
+        else:
+            bound, peak, unit = "tensor", 2.0 * pk["bf16_tflops"], "TOPS"
+        dtype = "int8"
     elif name.startswith("c4m"):
         m, n, k = int(name[3:]), 5120, 5120
         w = torch.randn((n, k), generator=gen, device=dev) * 0.02

@@ -163,6 +163,30 @@ int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* tiles, co
                   int group, int64_t M, int64_t N, int64_t K, const void* bias, int bias_dtype,
                   void* out, int64_t ldo, void* workspace, size_t workspace_bytes, void* stream);
 
+/* W4A8 grouped linear (int4_linear_a8, rdna2_ops/int4_weight_gemm_v07.py
+ * :476-537; float order of int4_model_switches_v07.py:19-34
+ * grouped_integer_reference): for each group g an exact integer dot
+ * e_g = sum a[m,k] * (q - z), total = total + fp32(e_g) * s[n,g] in group
+ * order (product and sum each rounded), y = total * a_scale[m] (+ bias[n]),
+ * fp32 out; integer != 0 writes sum_g e_g as int32 instead (bias and scales
+ * unused).  Weight format from b2_w4a8_prepare (a caller-owned pack of one
+ * PackedInt4):
+ *   tiles   u64 [ceil(N/128)][K/128][8][128] unsigned nibbles u = q + 8
+ *   groups  u64 [ceil(N/128)][K/group][128] = {fp32 scale, zu = z + 8}
+ * K a multiple of 128; group 32, 64 or 128. */
+size_t b2_w4a8_tiles_bytes(int64_t N, int64_t K);
+size_t b2_w4a8_groups_bytes(int64_t N, int64_t K, int group);
+int b2_w4a8_prepare(const void* data, int layout_kn, int order_high, const float* scales, const void* zeros,
+                    int64_t N, int64_t K, int group, void* tiles, void* groups, void* stream);
+/* Workspace (per-group activation sums) for b2_w4a8_gemm; rewritten every call. */
+size_t b2_w4a8_workspace_bytes(int64_t M, int64_t K, int group);
+/*   a        int8 [M,K], row stride lda bytes (multiple of 16), 16-byte aligned
+ *   a_scale  fp32 [M]; bias [N] of bias_dtype (0/1/2) or NULL
+ *   out      fp32 (integer: int32) [M, ldo] */
+int b2_w4a8_gemm(const void* a, int64_t lda, const void* tiles, const void* groups, int group, int64_t M,
+                 int64_t N, int64_t K, const float* a_scale, const void* bias, int bias_dtype, int integer,
+                 void* out, int64_t ldo, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Exact fp8 decode (rdna2_ops/fp8_weight_gemm_v06.py:22-46, 109-124):
  * w [rows, cols] of fp8_dtype (4 e4m3fn, 5 e5m2), row stride ld bytes ->
  * out of out_dtype (0 fp32, 1 fp16), row stride ldo elements. */

@@ -51,6 +51,7 @@ def lib():
         "b2o_pack_int4": [_p, _i64, _i64, _int, _int, _int, _p, _p, _p, _p],
         "b2o_dequant_int4": [_p, _p, _p, _i64, _i64, _int, _int, _p],
         "b2o_gemm_f32_f64": [_p, _i64, _p, _i64, _i64, _p, _int],
+        "b2o_w4a8_linear": [_p, _i64, _i64, _i64, _p, _i64, _p, _int, _p, _p, _int, _p, _p],
         "b2o_encode": [_p, _i64, _int, _p],
         "b2o_decode": [_p, _i64, _int, _p],
         "b2o_encode_e4m3": [_p, _i64, _p],
@@ -266,3 +267,21 @@ def gemm_f32_f64(a, w, threads=0):
     c = np.empty((m, n), np.float64)
     lib().b2o_gemm_f32_f64(_ptr(a), m, _ptr(w), n, k, _ptr(c), int(threads))
     return c
+
+
+def w4a8_linear(a8, centered, scales, group, sa, bias=None, integer=False):
+    """W4A8 grouped linear (reference grouped_integer_reference order):
+    a8 int8 [M,K], centered int8 [N,K] (= q - z), scales fp32 [N, K/group],
+    sa fp32 [M], bias fp32 [N] or None -> fp32 [M,N] (int32 when integer)."""
+    a8 = _c(a8, np.int8)
+    centered = _c(centered, np.int8)
+    scales = _c(scales, np.float32)
+    sa = _c(np.asarray(sa).reshape(-1), np.float32)
+    m, k = a8.shape
+    n = centered.shape[0]
+    b = None if bias is None else _c(np.asarray(bias).reshape(-1), np.float32)
+    out_f = np.zeros((m, n), np.float32)
+    out_i = np.zeros((m, n), np.int32)
+    lib().b2o_w4a8_linear(_ptr(a8), k, m, k, _ptr(centered), n, _ptr(scales), int(group), _ptr(sa),
+                          _ptr(b), int(bool(integer)), _ptr(out_f), _ptr(out_i))
+    return out_i if integer else out_f

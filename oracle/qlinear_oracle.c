@@ -449,6 +449,44 @@ void b2o_encode_e4m3(const float* x, int64_t n, uint8_t* out) {
 void b2o_decode_e4m3(const uint8_t* x, int64_t n, float* out) {
   for (int64_t i = 0; i < n; i++) out[i] = b2o_e4m3_to_f32(x[i]);
 }
+/*
+ * W4A8 grouped linear, restating rdna2-ops/int4_model_switches_v07.py:19-34
+ * (grouped_integer_reference) and the float order of the reference kernels
+ * (rdna2-ops/rdna2_ops/int4_weight_gemm_v07.py:194-216, enable_fp_fusion
+ * off): for every group g the integer dot e = sum_k a[m,k] * c[n,k] over
+ * the group's k (exact), total = total + fp32(e) * s[n,g] in group order
+ * (product and sum each rounded), y = total * sa[m], then + bias[n].
+ * integer != 0 returns the exact sum over all k instead (INTEGER mode).
+ * a [M,K] int8 (row stride lda); c [N,K] int8 centered weights q - z;
+ * s [N, K/G] fp32.
+ */
+void b2o_w4a8_linear(const int8_t* a, int64_t lda, int64_t M, int64_t K, const int8_t* c, int64_t N,
+                     const float* s, int G, const float* sa, const float* bias, int integer,
+                     float* out_f32, int32_t* out_i32) {
+  const int64_t ng = K / G;
+#pragma omp parallel for schedule(static)
+  for (int64_t m = 0; m < M; m++) {
+    for (int64_t n = 0; n < N; n++) {
+      float total = 0.0f;
+      int64_t exact_all = 0;
+      for (int64_t g = 0; g < ng; g++) {
+        int64_t e = 0;
+        for (int64_t k = g * G; k < (g + 1) * G; k++) e += (int64_t)a[m * lda + k] * (int64_t)c[n * K + k];
+        exact_all += e;
+        const float prod = (float)e * s[n * ng + g];
+        total = total + prod;
+      }
+      if (integer) {
+        out_i32[m * N + n] = (int32_t)exact_all;
+      } else {
+        float y = total * sa[m];
+        if (bias) y = y + bias[n];
+        out_f32[m * N + n] = y;
+      }
+    }
+  }
+}
+
 int b2o_max_threads(void) {
 #ifdef _OPENMP
   return omp_get_max_threads();

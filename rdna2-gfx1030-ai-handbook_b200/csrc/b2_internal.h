@@ -60,6 +60,17 @@ size_t w4a16_groups_bytes(int64_t N, int64_t K, int group);
 cudaError_t run_w4a16_prepare(const uint32_t* data, int layout_kn, int order_high, const float* scales,
                               const int32_t* zeros, int64_t N, int64_t K, int group, int dtype, uint32_t* tiles,
                               uint32_t* groups, cudaStream_t stream);
+// W4A8 grouped linear on the W4A8 tile format (see w4a8.cu); workspace holds
+// the per-group activation sums, w4a8_workspace(M, K, group) bytes.
+size_t w4a8_tiles_bytes(int64_t N, int64_t K);
+size_t w4a8_groups_bytes(int64_t N, int64_t K, int group);
+size_t w4a8_workspace(int64_t M, int64_t K, int group);
+cudaError_t run_w4a8_prepare(const uint32_t* data, int layout_kn, int order_high, const float* scales,
+                             const int32_t* zeros, int64_t N, int64_t K, int group, void* tiles, void* groups,
+                             cudaStream_t stream);
+cudaError_t run_w4a8(const int8_t* a, int64_t lda, const void* tiles, const void* groups, int group, int64_t M,
+                     int64_t N, int64_t K, const float* a_scale, const void* bias, int bias_dtype, int integer,
+                     void* out, int64_t ldo, void* workspace, cudaStream_t stream);
 cudaError_t run_pack_int4(const void* w, int w_dtype, int64_t ldw_el, int64_t N, int64_t K, int G,
                           int symmetric, int layout_kn, int order_high, int32_t* data, float* scales,
                           int32_t* zeros, int32_t* sums, cudaStream_t stream);

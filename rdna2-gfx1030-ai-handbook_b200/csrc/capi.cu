@@ -204,6 +204,47 @@ int b2_w4a16_gemm(const void* a, int a_dtype, int64_t lda, const void* tiles, co
                                         static_cast<cudaStream_t>(stream)));
 }
 
+size_t b2_w4a8_tiles_bytes(int64_t N, int64_t K) {
+  return (N > 0 && K >= 128 && K % 128 == 0 && N <= INT32_MAX && K <= INT32_MAX) ? b2::w4a8_tiles_bytes(N, K) : 0;
+}
+
+size_t b2_w4a8_groups_bytes(int64_t N, int64_t K, int group) {
+  if (N <= 0 || K < 128 || K % 128 || (group != 32 && group != 64 && group != 128)) return 0;
+  return b2::w4a8_groups_bytes(N, K, group);
+}
+
+size_t b2_w4a8_workspace_bytes(int64_t M, int64_t K, int group) {
+  if (M <= 0 || K < 128 || K % 128 || (group != 32 && group != 64 && group != 128)) return 0;
+  return b2::w4a8_workspace(M, K, group);
+}
+
+int b2_w4a8_prepare(const void* data, int layout_kn, int order_high, const float* scales, const void* zeros,
+                    int64_t N, int64_t K, int group, void* tiles, void* groups, void* stream) {
+  if (b2_w4a8_groups_bytes(N, K, group) == 0 || N * K >= (int64_t{1} << 31)) return fail();
+  if (!data || !scales || !zeros || !tiles || !groups) return fail();
+  if (!aligned16(tiles) || !aligned16(groups)) return fail();
+  return static_cast<int>(b2::run_w4a8_prepare(static_cast<const uint32_t*>(data), layout_kn != 0, order_high != 0,
+                                               scales, static_cast<const int32_t*>(zeros), N, K, group, tiles,
+                                               groups, static_cast<cudaStream_t>(stream)));
+}
+
+int b2_w4a8_gemm(const void* a, int64_t lda, const void* tiles, const void* groups, int group, int64_t M,
+                 int64_t N, int64_t K, const float* a_scale, const void* bias, int bias_dtype, int integer,
+                 void* out, int64_t ldo, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || M > INT32_MAX || M * N >= (int64_t{1} << 31)) return fail();
+  if (b2_w4a8_groups_bytes(N > 0 ? N : 1, K, group) == 0) return fail();
+  if (K * 128 * 15 >= (int64_t{1} << 31)) return fail();  // INT32 accumulator bound
+  if (M == 0 || N == 0) return 0;
+  if (!a || !tiles || !groups || !out || (!integer && !a_scale)) return fail();
+  if (!aligned16(a) || lda < K || lda % 16 || !aligned16(tiles) || !aligned16(groups) || ldo < N) return fail();
+  if (bias && (bias_dtype < 0 || bias_dtype > 2)) return fail();
+  const size_t need = b2_w4a8_workspace_bytes(M, K, group);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) return fail();
+  return static_cast<int>(b2::run_w4a8(static_cast<const int8_t*>(a), lda, tiles, groups, group, M, N, K, a_scale,
+                                       bias, bias_dtype, integer != 0, out, ldo, workspace,
+                                       static_cast<cudaStream_t>(stream)));
+}
+
 int b2_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld, int out_dtype,
                   void* out, int64_t ldo, void* stream) {
   if ((fp8_dtype != b2::kE4M3 && fp8_dtype != b2::kE5M2) || (out_dtype != b2::kF32 && out_dtype != b2::kF16))

@@ -45,6 +45,12 @@ SIGNATURES = {
     "b2_w4a16_gemm": ([_p, _int, _i64, _p, _p, _int, _i64, _i64, _i64, _p, _int, _p, _i64, _p, _size,
                        _p], _int),
     "b2_w4a16_tiles_bytes": ([_i64, _i64], _size),
+    "b2_w4a8_tiles_bytes": ([_i64, _i64], _size),
+    "b2_w4a8_groups_bytes": ([_i64, _i64, _int], _size),
+    "b2_w4a8_workspace_bytes": ([_i64, _i64, _int], _size),
+    "b2_w4a8_prepare": ([_p, _int, _int, _p, _p, _i64, _i64, _int, _p, _p, _p], _int),
+    "b2_w4a8_gemm": ([_p, _i64, _p, _p, _int, _i64, _i64, _i64, _p, _p, _int, _int, _p, _i64, _p, _size, _p],
+                     _int),
     "b2_w4a16_groups_bytes": ([_i64, _i64, _int], _size),
     "b2_w4a16_prepare": ([_p, _int, _int, _p, _p, _i64, _i64, _int, _int, _p, _p, _p], _int),
     "b2_fp8_decode": ([_p, _int, _i64, _i64, _i64, _int, _p, _i64, _p], _int),

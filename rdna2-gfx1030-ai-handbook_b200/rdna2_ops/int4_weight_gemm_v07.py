@@ -76,6 +76,22 @@ class W4A16Weight:
                            self.dtype)
 
 
+@dataclass
+class W4A8Weight:
+    """B200 W4A8 format (include/b2_qlinear.h, b2_w4a8_prepare): `tiles`
+    uint8 bytes of u64 [T, K/128, 8, 128] unsigned nibbles in the int8-unpack
+    order; `groups` u64 [T, K/group, 128] = {fp32 scale, zu}."""
+    tiles: torch.Tensor
+    groups: torch.Tensor
+    n: int
+    k: int
+    group_size: int
+
+    @property
+    def bytes(self):
+        return sum(t.numel() * t.element_size() for t in (self.tiles, self.groups))
+
+
 # ------------------------------------------------------------ CPU packer
 def pack_int4_cpu(w, *, group_size=64, symmetric=True, layout="nk", order="low"):
     """Independent CPU packer (reference int4_weight_gemm_v07.py:49-82):
@@ -284,3 +300,89 @@ def dense_linear(a, w, bias=None):
     kind = nat.KIND_BF16 if a.dtype == torch.bfloat16 else nat.KIND_F16
     return qgemm_raw(kind, a.view(torch.int16), w.view(torch.int16), ones_m, ones_n, bias,
                      nat.EPI_SEPARATE, out)
+
+
+# ------------------------------------------------------------------ W4A8
+_A8_METHODS = ("dot4", "dot4_words", "dot4_prepared", "dot4_split", "dot8")
+
+
+def prepare_w4a8(p):
+    """Caller-owned B200 W4A8 pack of a PackedInt4 (lossless: u = q + 8,
+    zu = z + 8, fp32 scales kept)."""
+    _validate(p)
+    if p.k % 128:
+        raise ValueError("W4A8 kernel needs K divisible by 128")
+    lib = nat.library()
+    tiles = torch.empty(lib.b2_w4a8_tiles_bytes(p.n, p.k), device=p.data.device, dtype=torch.uint8)
+    groups = torch.empty(lib.b2_w4a8_groups_bytes(p.n, p.k, p.group_size), device=p.data.device,
+                         dtype=torch.uint8)
+    nat.check(lib.b2_w4a8_prepare(
+        p.data.data_ptr(), int(p.layout == "kn"), int(p.order == "high"), p.scales.data_ptr(),
+        p.zeros.data_ptr(), p.n, p.k, p.group_size, tiles.data_ptr(), groups.data_ptr(),
+        nat.stream_ptr(p.data.device)), "b2_w4a8_prepare")
+    return W4A8Weight(tiles, groups, p.n, p.k, p.group_size)
+
+
+def int4_linear_a8(a, p, a_scale, *, bias=None, method="dot4", tile=(64, 64), num_warps=4,
+                   prepared=None, integer=False, return_kernel=False):
+    """Compute (A8 * row_scale) @ reconstructed W4.T, FP32 output
+    (reference int4_weight_gemm_v07.py:476-537).
+
+    Every method runs the tcgen05 kernel (csrc/w4a8.cu): per group an exact
+    INT32 dot, times the fp32 group scale, accumulated in fp32 in group order,
+    then times the row scale, plus bias -- bit-identical to the reference's
+    grouped order.  `prepared` may be a W4A8Weight (this package's caller-owned
+    pack); the reference's method-specific inputs (centered INT8 weight for
+    dot4_prepared, the dot8 activation tuple) are validated like the
+    reference and not needed.  integer=True returns the exact INT32 sum.
+    """
+    if isinstance(prepared, W4A8Weight):
+        wt = prepared
+    else:
+        _validate(p)
+        wt = None
+    n = wt.n if wt is not None else p.n
+    k = wt.k if wt is not None else p.k
+    nat.eager_only(a)
+    if (a.ndim != 2 or a.dtype != torch.int8 or a.device.type != "cuda" or a.shape[1] != k
+            or min(a.stride()) <= 0 or a.shape[0] * n >= 2**31):
+        raise ValueError("Matching A8[M,K] required")
+    m = a.shape[0]
+    if (not integer and (a_scale is None or a_scale.shape not in ((m,), (m, 1)) or a_scale.device != a.device
+                         or a_scale.dtype != torch.float32 or not a_scale.is_contiguous())):
+        raise ValueError("Contiguous FP32 per-activation-row scale required")
+    if bias is not None and (bias.shape != (n,) or bias.device != a.device or not bias.is_contiguous()
+                             or not bias.is_floating_point()):
+        raise ValueError("Floating bias [N] required")
+    if len(tile) != 2 or any(x not in (8, 16, 32, 64, 128) for x in tile) or num_warps not in (4, 8):
+        raise ValueError("Unsupported tile/warps")
+    if k * 128 * 15 >= 2**31:
+        raise ValueError("Integer accumulator bound exceeded")
+    if method not in _A8_METHODS:
+        raise ValueError(method)
+    if method in ("dot4", "dot4_prepared", "dot4_split") and min(tile) < 16:
+        raise ValueError("tl.dot tile dimensions must be >=16")
+    if method == "dot4_prepared" and not isinstance(prepared, W4A8Weight):
+        if (prepared is None or prepared.shape != (n, k) or prepared.dtype != torch.int8
+                or prepared.device != a.device):
+            raise ValueError("Centered INT8 prepared weight required")
+    if method == "dot8" and prepared is not None and not isinstance(prepared, W4A8Weight):
+        if not isinstance(prepared, tuple) or len(prepared) != 3:
+            raise ValueError("Dot8 prepared tuple required")
+    if wt is None:
+        wt = prepare_w4a8(p)
+    if a.stride(1) != 1 or a.stride(0) % 16 or a.data_ptr() % 16:
+        a = a.contiguous()  # K % 128 == 0, so contiguous rows are 16-byte multiples
+    dev = nat.require_device(a)
+    out = torch.empty((m, n), device=dev, dtype=torch.int32 if integer else torch.float32)
+    lib = nat.library()
+    need = lib.b2_w4a8_workspace_bytes(m, k, wt.group_size)
+    ws = torch.empty(max(need, 256), device=dev, dtype=torch.uint8)
+    sa = a_scale.reshape(-1) if a_scale is not None else None
+    nat.check(lib.b2_w4a8_gemm(
+        a.data_ptr(), a.stride(0) if m > 1 else k, wt.tiles.data_ptr(), wt.groups.data_ptr(), wt.group_size,
+        m, n, k, nat.ptr(sa), nat.ptr(bias), nat.DTYPE_CODE[bias.dtype] if bias is not None else 0,
+        int(bool(integer)), out.data_ptr(), n, ws.data_ptr(), ws.numel(), nat.stream_ptr(dev)),
+        "b2_w4a8_gemm")
+    kernel = {"name": "w4a8_kernel (tcgen05 kind::i8, swap-AB, per-group TMEM drain)", "arch": "sm_100a"}
+    return (out, kernel) if return_kernel else out

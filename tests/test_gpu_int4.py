@@ -210,3 +210,58 @@ def test_w4a16_workspace_reuse_leaves_counters_zero():
         y_fresh = i4.w4a16_gemm(a, wt)
         assert torch.equal(y_shared.view(torch.int16), y_fresh.view(torch.int16))
         assert int(ws[:4096].count_nonzero()) == 0  # the arrival counters
+
+
+# ------------------------------------------------------------------ W4A8
+def _packed_from_golden(z, key, n, k, g, layout, order):
+    f = {name: torch.from_numpy(z[key + "_" + name]) for name in ("data", "scales", "zeros", "sums")}
+    return i4.PackedInt4(f["data"], f["scales"], f["zeros"], f["sums"], n, k, g, False, layout, order).to("cuda")
+
+
+def test_w4a8_matches_reference_grouped_output(golden):
+    """int4_linear_a8 reproduces the reference's grouped_integer_reference
+    output (int4_model_switches_v07.py:19-34) bit for bit: g32 affine kn
+    pack, per-row scales, bias."""
+    z = golden("int4_packing.npz")
+    n, k = z["grouped_w"].shape
+    p = i4.PackedInt4(torch.from_numpy(z["grouped_data"]), torch.from_numpy(z["grouped_scales"]),
+                      torch.from_numpy(z["grouped_zeros"]), torch.zeros_like(torch.from_numpy(z["grouped_zeros"])),
+                      n, k, 32, False, "kn", "low").to("cuda")
+    a = torch.from_numpy(z["grouped_a"]).cuda()
+    sa = torch.from_numpy(z["grouped_sa"]).cuda()
+    bias = torch.from_numpy(z["grouped_bias"]).cuda()
+    y = i4.int4_linear_a8(a, p, sa, bias=bias)
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), z["grouped_y"].view(np.uint32))
+
+
+@pytest.mark.parametrize("g", [32, 64, 128])
+@pytest.mark.parametrize("sym", [True, False])
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+@pytest.mark.parametrize("order", ["low", "high"])
+def test_w4a8_integer_mode_matches_int_oracle(golden, g, sym, layout, order):
+    z = golden("int4_packing.npz")
+    key = f"g{g}_{'sym' if sym else 'aff'}_{layout}_{order}"
+    n, k = z["w"].shape
+    p = _packed_from_golden(z, key, n, k, g, layout, order)
+    a = torch.from_numpy(z["a"]).cuda()
+    y = i4.int4_linear_a8(a, p, None, integer=True)
+    assert np.array_equal(y.cpu().numpy().astype(np.int64), z[key + "_int_oracle"])
+
+
+@pytest.mark.parametrize("m", [1, 5, 16, 17, 33, 64, 100, 200])
+@pytest.mark.parametrize("g", [32, 64, 128])
+def test_w4a8_random_shapes_bit_exact(m, g):
+    """Ragged N (partial last row tile), token tiles 16/32/64 and several
+    token tiles, every group size: bit-exact against the oracle."""
+    n, k = 1000, 1152
+    gen = torch.Generator().manual_seed(20261105 + m + g)
+    w = torch.randn((n, k), generator=gen) * 0.05
+    p_cpu = i4.pack_int4_cpu(w, group_size=g, symmetric=False)
+    a = torch.randint(-128, 128, (m, k), generator=gen, dtype=torch.int8)
+    sa = torch.rand(m, generator=gen) * 0.02 + 0.001
+    bias = torch.randn(n, generator=gen) * 0.01
+    wt = i4.prepare_w4a8(p_cpu.to("cuda"))
+    y = i4.int4_linear_a8(a.cuda(), None, sa.cuda(), bias=bias.cuda(), prepared=wt)
+    c = i4.unpack_int4_cpu(p_cpu, floating=False).numpy().astype(np.int8)
+    ref = oracle.w4a8_linear(a.numpy(), c, p_cpu.scales.numpy(), g, sa.numpy(), bias.numpy())
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), ref.view(np.uint32))

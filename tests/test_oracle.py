@@ -177,3 +177,40 @@ def test_package_pack_int4_cpu_matches_golden(golden, g, sym):
             for f in ("data", "scales", "zeros", "sums"):
                 assert np.array_equal(getattr(p, f).numpy(), z[key + "_" + f]), (key, f)
             assert np.array_equal(unpack_int4_cpu(p, floating=False).numpy(), z[key + "_centered"])
+
+
+def _centered(data, zeros, n, k, g, layout, order):
+    """q - z from PackedInt4 storage (signed nibbles), numpy."""
+    words = data.view(np.uint32) if layout == "nk" else data.view(np.uint32).T
+    words = np.ascontiguousarray(words).astype(np.uint64)
+    shifts = np.arange(8, dtype=np.uint64) * 4
+    if order == "high":
+        shifts = 28 - shifts
+    q = ((words[..., None] >> shifts) & 15).astype(np.int32).reshape(n, k)
+    q = np.where(q >= 8, q - 16, q)
+    return (q - np.repeat(zeros, g, axis=1)).astype(np.int8)
+
+
+def test_w4a8_oracle_matches_reference_grouped_integer_reference(golden):
+    """The oracle's grouped W4A8 linear equals the reference's
+    grouped_integer_reference output (int4_model_switches_v07.py:19-34) bit
+    for bit (g32 affine "kn" pack, bias)."""
+    z = golden("int4_packing.npz")
+    a = z["grouped_a"]
+    n, k = z["grouped_w"].shape
+    c = _centered(z["grouped_data"], z["grouped_zeros"], n, k, 32, "kn", "low")
+    y = oracle.w4a8_linear(a, c, z["grouped_scales"], 32, z["grouped_sa"], z["grouped_bias"])
+    assert np.array_equal(y.view(np.uint32), z["grouped_y"].view(np.uint32))
+
+
+@pytest.mark.parametrize("g", [32, 64, 128])
+@pytest.mark.parametrize("layout", ["nk", "kn"])
+@pytest.mark.parametrize("order", ["low", "high"])
+def test_w4a8_oracle_integer_mode_matches_int_oracle(golden, g, layout, order):
+    z = golden("int4_packing.npz")
+    key = f"g{g}_aff_{layout}_{order}"
+    n, k = z["w"].shape
+    c = _centered(z[key + "_data"], z[key + "_zeros"], n, k, g, layout, order)
+    got = oracle.w4a8_linear(z["a"], c, z[key + "_scales"], g, np.ones(z["a"].shape[0], np.float32),
+                             integer=True)
+    assert np.array_equal(got.astype(np.int64), z[key + "_int_oracle"])
