@@ -54,7 +54,8 @@ def parse():
     ap.add_argument("--sets", type=int, default=4, help="input sets cycled to defeat L2 reuse")
     ap.add_argument("--workload", default="c2",
                     help="c2 (headline, default), c1, c3m1/c3m16/c3m128/c3m2048 (W4A16), "
-                         "c4m1/c4m2048 (FP8); non-c2 workloads run on one GPU")
+                         "c4m1/c4m2048 (FP8), w4a8m<M> (W4A8), c5 (28-block W8A8 DiT stack); "
+                         "non-c2 workloads run on one GPU")
     return ap.parse_args()
 
 
@@ -440,6 +441,7 @@ def run_workload(args):
     name = args.workload
     sets = max(args.sets, 8)
     graph_ok = False
+    per_graph_override = None
     if name == "c1":
         m, n, k = 1024, 3072, 3072
         xs = [(torch.randn((m, k), generator=gen, device=dev)).half() for _ in range(sets)]
@@ -535,6 +537,70 @@ def run_workload(args):
         else:
             bound, peak, unit = "tensor", 2.0 * pk["bf16_tflops"], "TFLOP/s"
         dtype = "e4m3"
+    elif name == "c5":
+        # Config 5: 28 DiT blocks, hidden 3072, MLP ratio 4, every linear W8A8
+        # with block-128 rotation; fp16 activations [8192, 3072] ~N(0,1).
+        # Linears only (attention is not on the path): QKV, then the out
+        # projection on the Q third (a strided view, row stride 9216), up,
+        # down; the down output feeds the next block.  Weights ~N(0, 1/K)
+        # keep the activations O(1) through the 28 blocks.  One step = the
+        # whole stack, 112 fused linears; 3.2 GB of int8 weights (> L2).
+        m, hid, blocks = 8192, 3072, 28
+        shapes = ((3 * hid, hid), (hid, hid), (4 * hid, hid), (hid, 4 * hid))
+        layers = []
+        for _ in range(blocks):
+            blk = []
+            for n_, k_ in shapes:
+                w = torch.randn((n_, k_), generator=gen, device=dev) * (1.0 / k_ ** 0.5)
+                wq, sw = qlinear.quantize_weight(w, rotation_block=ROT)
+                blk.append((wq, sw, n_, k_))
+                del w
+            layers.append(blk)
+        x0 = torch.randn((m, hid), generator=gen, device=dev).half()
+        bufs = {"qkv": torch.empty((m, 3 * hid), device=dev, dtype=torch.float16),
+                "o": torch.empty((m, hid), device=dev, dtype=torch.float16),
+                "h": torch.empty((m, 4 * hid), device=dev, dtype=torch.float16),
+                "x": torch.empty((m, hid), device=dev, dtype=torch.float16)}
+        lib = nat.library()
+        ws_bytes = lib.b2_quant_linear_workspace_bytes(m, 4 * hid)
+        ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+        # (input, its row stride, output) per linear of a block
+        wiring = ((None, hid, "qkv"), ("qkv", 3 * hid, "o"), ("o", hid, "h"), ("h", 4 * hid, "x"))
+
+        def raw_linear(x_ptr, ldx, wq, sw, n_, k_, out):
+            nat.check(lib.b2_quant_linear(nat.KIND_I8, x_ptr, nat.F16, m, k_, ldx, ROT, wq.data_ptr(), k_, n_,
+                                          sw.data_ptr(), sw.numel(), None, 0, nat.EPI_SEPARATE, out.data_ptr(),
+                                          nat.F16, n_, ws.data_ptr(), ws_bytes, nat.stream_ptr(dev)),
+                      "b2_quant_linear")
+
+        def step(i):
+            for b, blk in enumerate(layers):
+                for (src, ldx, dst), (wq, sw, n_, k_) in zip(wiring, blk):
+                    x = (x0 if b == 0 else bufs["x"]) if src is None else bufs[src]
+                    raw_linear(x.data_ptr(), ldx, wq, sw, n_, k_, bufs[dst])
+
+        # the public call on the first QKV and on the strided out-projection
+        # input, against the raw calls the stack makes
+        wq, sw, n_, k_ = layers[0][0]
+        ref = rdna2_ops.w8a8_linear(x0, wq, sw, None, rotation_block=ROT, out_dtype=torch.float16)
+        raw_linear(x0.data_ptr(), hid, wq, sw, n_, k_, bufs["qkv"])
+        torch.cuda.synchronize()
+        assert torch.equal(bufs["qkv"].view(torch.int16), ref.view(torch.int16)), "raw QKV differs from public call"
+        wq, sw, n_, k_ = layers[0][1]
+        ref = rdna2_ops.w8a8_linear(bufs["qkv"][:, :hid], wq, sw, None, rotation_block=ROT, out_dtype=torch.float16)
+        raw_linear(bufs["qkv"].data_ptr(), 3 * hid, wq, sw, n_, k_, bufs["o"])
+        torch.cuda.synchronize()
+        assert torch.equal(bufs["o"].view(torch.int16), ref.view(torch.int16)), "raw out-proj differs from public call"
+        step(0)
+        torch.cuda.synchronize()
+        assert bool(torch.isfinite(bufs["x"]).all()), "stack output not finite"
+        graph_ok, per_graph_override = True, 1
+        metric = "W8A8 DiT stack TOPS (config 5, 28 blocks, rotated)"
+        flops = 2.0 * m * sum(n_ * k_ for n_, k_ in shapes) * blocks  # 51.95 TOP
+        launches = 2 * 4 * blocks
+        bound, peak, unit, traffic = "tensor", 2.0 * pk["bf16_tflops"], "TOPS", None
+        dtype = "int8"
+        n, k = hid, hid
     else:
         raise SystemExit(f"unknown workload {name}")
     for i in range(max(3, args.warmup)):
@@ -546,7 +612,7 @@ def run_workload(args):
         # Launch-bound small shapes: the timed steps replay one CUDA graph of
         # `per_graph` back-to-back C-ABI calls (cycling the weight copies), so
         # the device time is the kernels' own, not the host's launch rate.
-        per_graph = sets * 4
+        per_graph = per_graph_override or sets * 4
         replays = max(1, -(-args.steps // per_graph))
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
@@ -579,7 +645,9 @@ def run_workload(args):
     line = {"workload": name, "metric": metric, "value": round(value, 2), "unit": "TOPS" if dtype == "int8" else "TFLOP/s",
             "n_gpus": 1, "steps": steps_timed, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
             "higher_is_better": True, "dtype": dtype, "data": "synthetic",
-            "config": {"M": m, "N": n, "K": k, "l2": f"weights cycled over {sets} copies"},
+            "config": ({"M": m, "hidden": 3072, "blocks": 28, "linears": "QKV 9216x3072, out 3072x3072, "
+                        "up 12288x3072, down 3072x12288, block-128 rotation", "l2": "3.2 GB of weights per step"}
+                       if name == "c5" else {"M": m, "N": n, "K": k, "l2": f"weights cycled over {sets} copies"}),
             "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": unit,
                          "frac": round(achieved / peak, 4), "algorithmic_bytes": traffic,
                          "peak_source": pk["source"]},

@@ -52,8 +52,10 @@ int b2_pair_capacity(void);
 /* Process-wide GEMM kernel selection: 0 = automatic (pair or single tiles by
  * a persistent-wave time model), 1 = single-CTA kernel, 2 = pair kernel (both
  * with automatic N tile), 3 = single N=256, 4 = single N=128, 5 = pair
- * N=256, 6 = pair N=192.  A tuning and verification knob; results are
- * identical for every choice.
+ * N=256, 6 = pair N=192, 7 = pair N=256 with the output staged in shared
+ * memory and written by TMA stores (automatic choice for pair tiles whose
+ * output rows are 16-byte aligned; 5 otherwise).  A tuning and verification
+ * knob; results are identical for every choice.
  * No reference counterpart (the reference exposes tile keywords instead,
  * rdna2_ops/int8_gemm.py:195-214). */
 int b2_set_gemm_path(int path);

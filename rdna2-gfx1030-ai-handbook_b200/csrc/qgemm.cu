@@ -22,7 +22,10 @@
 //               accumulators.
 //   warps 2..5  epilogue: double-buffered TMEM accumulators let tile t+1's
 //               MMAs overlap tile t's epilogue; tcgen05.ld ping-pong buffers,
-//               per-token x per-channel scale, bias and cast, 16-byte stores.
+//               per-token x per-channel scale, bias and cast; the pair
+//               kernel stages each 32-row x 128-byte unit in swizzled shared
+//               memory and writes it with a TMA store (6-stage ring), or,
+//               for unaligned outputs, stores 16 bytes per lane (7 stages).
 //
 // Epilogue rounding follows the reference exactly:
 //   separate  float(acc)*(sa*sb) then + bias in fp32, two roundings
@@ -31,6 +34,7 @@
 //   kitchen   (float(acc)*(sa*sb)).to(out) + bias.to(out)
 //             (production/MOSS_RDNA2_INT8/backend.py:128-143)
 //   none      raw INT32 accumulator              (int8_matmul, :195-200)
+#include <cstring>
 #include <mutex>
 
 #include "b2_common.cuh"
@@ -61,16 +65,23 @@ __host__ __device__ constexpr uint32_t tmem_cols_for(int cols) {
   return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512;
 }
 
-// Shared-memory plan: A ring, B ring, per-warp staging of one 32-column chunk
-// of epilogue scale/bias, barriers.
-template <int A_ROWS, int B_ROWS, int BN, int STAGES>
+// Output staging of the TMA-store epilogue: per epilogue warp, two 4 KiB
+// buffers of 32 rows x 128 bytes (128-byte swizzled, the layout the store's
+// tensor map reads).
+constexpr int kOutBufBytes = 32 * 128;
+constexpr int kOutStageBytes = kEpiWarps * 2 * kOutBufBytes;
+
+// Shared-memory plan: A ring, B ring, optional output staging, per-warp
+// staging of one 32-column chunk of epilogue scale/bias, barriers.
+template <int A_ROWS, int B_ROWS, int BN, int STAGES, int OUT_STAGE = 0>
 struct Smem {
   static constexpr int kABytes = A_ROWS * 128;
   static constexpr int kBBytes = B_ROWS * 128;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kOffA = 0;
   static constexpr int kOffB = STAGES * kABytes;
-  static constexpr int kOffEpi = STAGES * kStageBytes;
+  static constexpr int kOffOut = STAGES * kStageBytes;  // 1 KiB aligned (stage sizes are)
+  static constexpr int kOffEpi = kOffOut + OUT_STAGE;
   static constexpr int kOffBar = kOffEpi + kEpiWarps * 64 * 4;
   static constexpr int kNumBars = 2 * STAGES + 4;
   static constexpr int kOffMisc = kOffBar + kNumBars * 8;
@@ -118,14 +129,12 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, int out) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// One thread, one output row, 32 consecutive columns starting at n; the
-// chunk's per-channel scales and bias come from this warp's shared staging.
+// Epilogue values of one thread's 32 accumulator columns; the chunk's
+// per-channel scales and bias come from this warp's shared staging.
 template <int KIND, int MODE, int OUT>
-__device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t (&r)[32], int row,
-                                            int n, float sa, const float* csb, const float* cbias) {
-  if (row >= p.M) return;
+__device__ __forceinline__ void chunk_values(const GemmParams& p, const uint32_t (&r)[32], float sa,
+                                             const float* csb, const float* cbias, float (&v)[32]) {
   const bool hb = p.bias != nullptr;
-  float v[32];
 #pragma unroll
   for (int j = 0; j < 32; j += 4) {
     const float4 s4 = *reinterpret_cast<const float4*>(csb + j);
@@ -141,6 +150,16 @@ __device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t 
       }
     }
   }
+}
+
+// One thread, one output row, 32 consecutive columns starting at n, stored
+// straight to global memory.
+template <int KIND, int MODE, int OUT>
+__device__ __forceinline__ void store_chunk(const GemmParams& p, const uint32_t (&r)[32], int row,
+                                            int n, float sa, const float* csb, const float* cbias) {
+  if (row >= p.M) return;
+  float v[32];
+  chunk_values<KIND, MODE, OUT>(p, r, sa, csb, cbias, v);
   const int64_t base = static_cast<int64_t>(row) * p.ldc + n;
   if (p.vec_ok && n + 32 <= p.N) {
     if constexpr (OUT == kF32 || OUT == kI32) {
@@ -187,6 +206,52 @@ __device__ __forceinline__ void store_dispatch(const GemmParams& p, const uint32
     case kEpiKitchen * 4 + kF32: store_chunk<KIND, kEpiKitchen, kF32>(p, r, row, n, sa, csb, cb); break;
     case kEpiKitchen * 4 + kF16: store_chunk<KIND, kEpiKitchen, kF16>(p, r, row, n, sa, csb, cb); break;
     case kEpiKitchen * 4 + kBF16: store_chunk<KIND, kEpiKitchen, kBF16>(p, r, row, n, sa, csb, cb); break;
+    default: break;
+  }
+}
+
+// One thread, one staging row (32 rows x 128 bytes, 128-byte swizzle: the
+// 16-byte piece j of row r sits at piece j ^ (r % 8)), 32 columns written at
+// piece offset piece0 (16-bit outputs fill a row with two chunks, 32-bit
+// outputs with one).  The swizzle keeps each quarter-warp's 16-byte stores on
+// distinct banks.
+template <int KIND, int MODE, int OUT>
+__device__ __forceinline__ void stage_chunk(const GemmParams& p, const uint32_t (&r)[32], uint32_t row_addr,
+                                            int lane, int piece0, float sa, const float* csb,
+                                            const float* cbias) {
+  float v[32];
+  chunk_values<KIND, MODE, OUT>(p, r, sa, csb, cbias, v);
+  const uint32_t sw = static_cast<uint32_t>(lane & 7);
+  if constexpr (OUT == kF32 || OUT == kI32) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      sts_v4(row_addr + ((static_cast<uint32_t>(j + piece0) ^ sw) << 4),
+             make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                        __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3])));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      sts_v4(row_addr + ((static_cast<uint32_t>(j + piece0) ^ sw) << 4),
+             make_uint4(pack2(v[8 * j], v[8 * j + 1], OUT), pack2(v[8 * j + 2], v[8 * j + 3], OUT),
+                        pack2(v[8 * j + 4], v[8 * j + 5], OUT), pack2(v[8 * j + 6], v[8 * j + 7], OUT)));
+  }
+}
+
+template <int KIND>
+__device__ __forceinline__ void stage_dispatch(const GemmParams& p, const uint32_t (&r)[32], uint32_t row_addr,
+                                               int lane, int piece0, float sa, const float* csb,
+                                               const float* cb) {
+  switch (p.epilogue * 4 + p.out_dtype) {
+    case kEpiNone * 4 + kI32: stage_chunk<KIND, kEpiNone, kI32>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
+    case kEpiSeparate * 4 + kF32: stage_chunk<KIND, kEpiSeparate, kF32>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
+    case kEpiSeparate * 4 + kF16: stage_chunk<KIND, kEpiSeparate, kF16>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
+    case kEpiSeparate * 4 + kBF16: stage_chunk<KIND, kEpiSeparate, kBF16>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
+    case kEpiFma * 4 + kF32: stage_chunk<KIND, kEpiFma, kF32>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
+    case kEpiFma * 4 + kF16: stage_chunk<KIND, kEpiFma, kF16>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
+    case kEpiFma * 4 + kBF16: stage_chunk<KIND, kEpiFma, kBF16>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
+    case kEpiKitchen * 4 + kF32: stage_chunk<KIND, kEpiKitchen, kF32>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
+    case kEpiKitchen * 4 + kF16: stage_chunk<KIND, kEpiKitchen, kF16>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
+    case kEpiKitchen * 4 + kBF16: stage_chunk<KIND, kEpiKitchen, kBF16>(p, r, row_addr, lane, piece0, sa, csb, cb); break;
     default: break;
   }
 }
@@ -250,6 +315,73 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tadd
     __syncwarp();
     if (c + 2 < NC) load_col(p, n0 + (c + 2) * 32 + lane, sb0, sb_n, b_n);
     store_dispatch<KIND>(p, r1, row, n0 + (c + 1) * 32, sa, wst, wst + 32);
+    __syncwarp();
+    if (c + 2 < NC) tmem_ld_wait(r0);
+  }
+}
+
+// The same epilogue with the output staged through shared memory: each
+// 128-byte-wide column unit of the warp's 32 rows is written into one of two
+// swizzled staging buffers and leaves as one TMA store (whole 128-byte lines
+// to L2 instead of 32 half-sector stores per instruction), while the next
+// unit is converted.  Lane 0 issues and waits on the warp's bulk groups; the
+// tensor map clips rows >= M and columns >= N.
+template <int KIND, int BN, typename Release>
+__device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const CUtensorMap* tma_c, uint32_t taddr,
+                                                  int row, int row0, int n0, int lane, float* wst,
+                                                  uint32_t obuf, uint32_t& ob_sel, Release release) {
+  constexpr int NC = BN / 32;
+  static_assert(NC % 2 == 0, "ping-pong over chunk pairs");
+  const int uc = (p.out_dtype == kF16 || p.out_dtype == kBF16) ? 2 : 1;  // chunks per staging row
+  const float sb0 = (p.sb != nullptr && p.sb_scalar) ? p.sb[0] : 0.0f;
+  const float sa = (p.sa != nullptr && row < p.M) ? p.sa[row] : 0.0f;
+  auto emit = [&](const uint32_t (&r)[32], int c) {
+    const int part = c & (uc - 1);
+    if (part == 0) {
+      if (lane == 0) bulk_wait_read<1>();  // the buffer's previous store has read it
+      __syncwarp();
+    }
+    const uint32_t buf = obuf + ob_sel * static_cast<uint32_t>(kOutBufBytes);
+    stage_dispatch<KIND>(p, r, buf + static_cast<uint32_t>(lane) * 128u, lane, part * 4, sa, wst, wst + 32);
+    if (part == uc - 1) {
+      fence_proxy_async_smem();  // generic-proxy writes visible to the TMA
+      __syncwarp();
+      const int x = n0 + (c - part) * 32;
+      if (lane == 0 && row0 < p.M && x < p.N) {
+        tma_store_2d(tma_c, buf, x, row0);
+        bulk_commit_group();
+      }
+      ob_sel ^= 1u;
+    }
+  };
+  float sb_n, b_n;
+  load_col(p, n0 + lane, sb0, sb_n, b_n);
+  uint32_t r0[32], r1[32];
+  __syncwarp();
+  tmem_ld32(taddr, r0);
+  tmem_ld_wait(r0);
+#pragma unroll 1
+  for (int c = 0; c < NC; c += 2) {
+    __syncwarp();
+    wst[lane] = sb_n;
+    wst[32 + lane] = b_n;
+    __syncwarp();
+    load_col(p, n0 + (c + 1) * 32 + lane, sb0, sb_n, b_n);
+    tmem_ld32(taddr + static_cast<uint32_t>((c + 1) * 32), r1);
+    emit(r0, c);
+    __syncwarp();
+    tmem_ld_wait(r1);
+    if (c + 2 < NC) {
+      tmem_ld32(taddr + static_cast<uint32_t>((c + 2) * 32), r0);
+    } else {
+      release();  // all TMEM reads of this tile are complete
+    }
+    __syncwarp();
+    wst[lane] = sb_n;
+    wst[32 + lane] = b_n;
+    __syncwarp();
+    if (c + 2 < NC) load_col(p, n0 + (c + 2) * 32 + lane, sb0, sb_n, b_n);
+    emit(r1, c + 1);
     __syncwarp();
     if (c + 2 < NC) tmem_ld_wait(r0);
   }
@@ -414,11 +546,12 @@ __global__ void __launch_bounds__(192, 1)
 // and signals both CTAs' `empty` / `tfull` barriers with one commit each;
 // both epilogues hand TMEM back through the leader's `tempty` barrier (8
 // arrivals).
-template <int KIND, int BN, int STAGES>
+template <int KIND, int BN, int STAGES, bool TSTORE>
 __global__ void __launch_bounds__(192, 1)
     qgemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
-                      const __grid_constant__ CUtensorMap tma_b, const GemmParams p) {
-  using L = Smem<128, BN / 2, BN, STAGES>;
+                      const __grid_constant__ CUtensorMap tma_b,
+                      const __grid_constant__ CUtensorMap tma_c, const GemmParams p) {
+  using L = Smem<128, BN / 2, BN, STAGES, TSTORE ? kOutStageBytes : 0>;
   constexpr int kKbElems = (KIND == kKindBF16 || KIND == kKindF16) ? 64 : 128;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -546,6 +679,8 @@ __global__ void __launch_bounds__(192, 1)
     const int quarter = warp & 3;
     float* wsb = reinterpret_cast<float*>(smem + L::kOffEpi) + (warp - 2) * 64;
     const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint32_t obuf = smem_u32(smem + L::kOffOut) + static_cast<uint32_t>((warp - 2) * 2 * kOutBufBytes);
+    uint32_t ob_sel = 0;
     int t = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++t) {
       const int buf = t & 1;
@@ -557,12 +692,22 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
-      const int row = tm * 256 + static_cast<int>(rank) * 128 + quarter * 32 + lane;
-      epilogue_tile<KIND, BN>(p, taddr, row, tn * BN, lane, wsb, [&] {
+      const int row0 = tm * 256 + static_cast<int>(rank) * 128 + quarter * 32;
+      auto release = [&] {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(tempty_leader + static_cast<uint32_t>(buf * 8));
-      });
+      };
+      if constexpr (TSTORE) {
+        epilogue_tile_tma<KIND, BN>(p, &tma_c, taddr, row0 + lane, row0, tn * BN, lane, wsb, obuf, ob_sel,
+                                    release);
+      } else {
+        epilogue_tile<KIND, BN>(p, taddr, row0 + lane, tn * BN, lane, wsb, release);
+      }
+    }
+    if constexpr (TSTORE) {
+      if (lane == 0) bulk_wait_all();  // staging reads and global writes done
+      __syncwarp();
     }
   }
 
@@ -612,6 +757,22 @@ static cudaError_t make_kmajor_map(CUtensorMap* map, const void* ptr, int elem_b
                   2, const_cast<void*>(ptr), dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+// Output map of the TMA-store epilogue: dims {N, M}, box {128 bytes of
+// columns, 32 rows}, 128-byte swizzle (the staging layout).
+static cudaError_t make_out_map(CUtensorMap* map, void* ptr, int elem_bytes, int64_t cols, int64_t rows,
+                                int64_t row_stride_bytes) {
+  EncodeTiledFn fn = encoder();
+  if (fn == nullptr) return cudaErrorNotSupported;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_stride_bytes)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem_bytes), 32u};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, ptr,
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
@@ -666,11 +827,11 @@ static cudaError_t launch_single(const void* a, int64_t lda, const void* b, int6
   return cudaGetLastError();
 }
 
-template <int KIND, int BN, int STAGES>
+template <int KIND, int BN, int STAGES, bool TSTORE>
 static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams p,
                                int max_ctas, cudaStream_t stream) {
-  using L = Smem<128, BN / 2, BN, STAGES>;
-  auto kernel = qgemm_pair_kernel<KIND, BN, STAGES>;
+  using L = Smem<128, BN / 2, BN, STAGES, TSTORE ? kOutStageBytes : 0>;
+  auto kernel = qgemm_pair_kernel<KIND, BN, STAGES, TSTORE>;
   static bool configured[64] = {false};
   static int max_pairs[64] = {0};
   cudaError_t e = configure_once(kernel, L::kAlloc, configured);
@@ -701,6 +862,13 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
   CUtensorMap ma, mb;
   if ((e = make_kmajor_map(&ma, a, eb, p.K, p.M, lda * eb, 128)) != cudaSuccess) return e;
   if ((e = make_kmajor_map(&mb, b, eb, p.K, p.N, ldb * eb, BN / 2)) != cudaSuccess) return e;
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  if (TSTORE) {
+    const int ob = (p.out_dtype == kF16 || p.out_dtype == kBF16) ? 2 : 4;
+    if (!p.vec_ok) return cudaErrorInvalidValue;
+    if ((e = make_out_map(&mc, p.out, ob, p.N, p.M, p.ldc * ob)) != cudaSuccess) return e;
+  }
   p.tiles_m = static_cast<int>((p.M + 255) / 256);
   p.tiles_n = static_cast<int>((p.N + BN - 1) / BN);
   const int tiles = p.tiles_m * p.tiles_n;
@@ -708,7 +876,7 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
   if (max_ctas > 0 && max_ctas / 2 < pairs) pairs = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
   if (tiles < pairs) pairs = tiles;
   cfg.gridDim = dim3(2 * pairs);
-  e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
+  e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, p);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
@@ -716,7 +884,7 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
 // persistent grid size in pairs), or -1 when cluster launch is unavailable.
 int pair_capacity() {
   using L = Smem<128, 128, 256, 7>;
-  auto kernel = qgemm_pair_kernel<kKindI8, 256, 7>;
+  auto kernel = qgemm_pair_kernel<kKindI8, 256, 7, false>;
   static bool configured[64] = {false};
   static int cap[64] = {0};
   const int dev = current_device();
@@ -762,7 +930,8 @@ static int choose_config(int64_t M, int64_t N) {
 }
 
 // Kernel selection: 0 auto; 1 single-CTA (auto N tile); 2 pair (auto N tile);
-// 3 single BN=256; 4 single BN=128; 5 pair BN=256; 6 pair BN=192.
+// 3 single BN=256; 4 single BN=128; 5 pair BN=256; 6 pair BN=192;
+// 7 pair BN=256 with the TMA-store epilogue (needs 16-byte aligned output rows).
 static int g_force_path = 0;
 
 template <int KIND>
@@ -773,8 +942,10 @@ static cudaError_t dispatch(int cfg, const void* a, int64_t lda, const void* b, 
     case 4: return launch_single<KIND, 128, 6>(a, lda, b, ldb, p, max_ctas, stream);
     // 7 stages: the ring covers the ~2k-cycle refill (TMA after the slot's
     // MMAs complete) at 512 tensor cycles per k-block; 6 left a bubble per wrap.
-    case 5: return launch_pair<KIND, 256, 7>(a, lda, b, ldb, p, max_ctas, stream);
-    case 6: return launch_pair<KIND, 192, 7>(a, lda, b, ldb, p, max_ctas, stream);
+    case 5: return launch_pair<KIND, 256, 7, false>(a, lda, b, ldb, p, max_ctas, stream);
+    case 6: return launch_pair<KIND, 192, 7, false>(a, lda, b, ldb, p, max_ctas, stream);
+    // 6 stages + 32 KiB of output staging
+    case 7: return launch_pair<KIND, 256, 6, true>(a, lda, b, ldb, p, max_ctas, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -789,9 +960,16 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
   int cfg = g_force_path;
   const int64_t tm = (p.M + 127) / 128;
   const bool wide = p.N > 128 && tm * ((p.N + 255) / 256) >= device_sm_count() / 2;
-  if (cfg == 0) cfg = choose_config(p.M, p.N);
+  if (cfg == 0) {
+    cfg = choose_config(p.M, p.N);
+    // Staged TMA stores: whole 128-byte lines instead of 32 half-sector
+    // stores per warp instruction; on the config-2 GEMM 107.5 us against
+    // 129.0 us for the 7-stage st.global epilogue on the same box.
+    if (cfg == 5 && p.vec_ok) cfg = 7;
+  }
   if (cfg == 2) cfg = 5;
   if (cfg == 1) cfg = wide ? 3 : 4;
+  if (cfg == 7 && !p.vec_ok) cfg = 5;  // TMA stores need 16-byte aligned output rows
   cudaError_t e = kind == kKindI8     ? dispatch<kKindI8>(cfg, a, lda, b, ldb, p, max_ctas, stream)
                   : kind == kKindE4M3 ? dispatch<kKindE4M3>(cfg, a, lda, b, ldb, p, max_ctas, stream)
                   : kind == kKindF16  ? dispatch<kKindF16>(cfg, a, lda, b, ldb, p, max_ctas, stream)

@@ -33,10 +33,12 @@ FLOAT_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
 def set_gemm_path(path):
     """Process-wide GEMM kernel choice: "auto", "single" (1-CTA 128-row
     tiles), "pair" (2-CTA cta_group::2 256-row tiles), or a fixed tile:
-    "single256", "single128", "pair256", "pair192".  Results are
-    bit-identical; this is a tuning and verification knob."""
+    "single256", "single128", "pair256", "pair192", "pair256s" (pair tiles
+    with the output staged in shared memory and written by TMA stores; falls
+    back to "pair256" for outputs whose rows are not 16-byte aligned).
+    Results are bit-identical; this is a tuning and verification knob."""
     code = {"auto": 0, "single": 1, "pair": 2, "single256": 3, "single128": 4, "pair256": 5,
-            "pair192": 6}[path]
+            "pair192": 6, "pair256s": 7}[path]
     nat.check(nat.library().b2_set_gemm_path(code), "b2_set_gemm_path")
 
 
