@@ -60,6 +60,15 @@ int b2_pair_capacity(void);
  * rdna2_ops/int8_gemm.py:195-214). */
 int b2_set_gemm_path(int path);
 
+/* Process-wide activation-prologue kernel selection: 0 = automatic (the
+ * lane-block kernel where it applies), 1 = the warp-shuffle kernel (every
+ * mode), 2 = the lane-block kernel: one lane per 64 elements, INT8
+ * ties-to-even codes of fp32/fp16/bf16 rows with K % 64 == 0, rotation
+ * blocks <= 2048 and 16-byte aligned input and code rows (other
+ * calls fall back to 1).  A tuning and verification knob; codes and scales
+ * are identical for every choice.  No reference counterpart. */
+int b2_set_prologue_path(int path);
+
 /* SYNCHRONOUS: read (and if reset != 0 clear) the device status word that a
  * kernel sets when one of its bounded waits gives up (0 = no failure; else
  * 0x100 | site).  Call after synchronizing the stream. */

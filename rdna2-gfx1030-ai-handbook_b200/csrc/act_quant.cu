@@ -6,7 +6,15 @@
 // production/MOSS_RDNA2_INT8/backend.py:112-122 and the row quantizer
 // _quant_rows of rdna2_ops/fp8_weight_gemm_v06.py:76-92 (ties to even here).
 //
-// Layout: a row is split into 256-element segments; lane l of a warp holds
+// Two kernels give bit-identical codes and scales:
+//   act_quant_lane_kernel  INT8 ties-to-even codes of 16/32-bit rows with
+//                          K % 64 == 0 (the production path): one lane per
+//                          64-element slice, butterflies below 64 inside the
+//                          lane, an exact FMA-corrected quantizer.
+//   act_quant_kernel       every mode (e4m3, the reference's _quant_rows,
+//                          fp8 inputs, ragged or unaligned rows), below.
+//
+// act_quant_kernel layout: a row is split into 256-element segments; lane l of a warp holds
 // elements [seg*256 + 8l, seg*256 + 8l + 8) of each of its SPW segments in
 // registers (one 16-byte load per segment for 16-bit inputs).  WPR warps share
 // a row when K > 16 segments.  The butterfly stages run in the fixed order
@@ -285,6 +293,250 @@ __global__ void __launch_bounds__(128)
   }
 }
 
+// ------------------------------------------------------- lane-block kernel
+// INT8 (ties-to-even) prologue with one lane per E-element slice of a row:
+// every butterfly stage below E runs inside the lane (one add or subtract
+// per element, no shuffles), stages E..block/2 exchange with the lane
+// (h / E) away, and the per-row absmax meets in shared memory.  Rows of
+// TPR = K / E lanes are packed R to a CTA.
+//
+// Quantization is exact without a slow path: with r = RN(1/s) (correctly
+// rounded reciprocal), y = RN(v*r) is a faithful approximation of v/s, the
+// residual e = v - s*y is exact in one fma, and RN(y + e*r) is the correctly
+// rounded quotient RN(v/s) (Markstein's theorem, IBM J. Res. Dev. 34(1),
+// 1990; Muller et al., Handbook of Floating-Point Arithmetic, 2nd ed.,
+// section 5.1).  Its conditions (no overflow, no underflow of the residual
+// for quotients that can reach 1/2) hold for s in [2^-60, 2^60]; rows
+// outside that range are rescaled by an exact power of two (2^64 or 2^-64,
+// applied to v and s alike), which leaves every quotient that can round
+// away from zero unchanged.  Rows with a non-finite scale use the IEEE
+// division per element.  E = 64 elements per lane; a CTA holds whole rows
+// (about 128 threads, at most kLaneThreads), several CTAs per SM.
+constexpr int kLaneE = 64;
+constexpr int kLaneThreads = 384;
+
+template <int DT, int E>
+__device__ __forceinline__ void load_slice(const void* x, int64_t off, bool live, float (&v)[E]) {
+  if (!live) {
+#pragma unroll
+    for (int i = 0; i < E; ++i) v[i] = 0.0f;
+    return;
+  }
+  if constexpr (DT == kF32) {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const float*>(x) + off);
+#pragma unroll
+    for (int j = 0; j < E / 4; ++j) {
+      const uint4 w = __ldg(p + j);
+      v[4 * j] = __uint_as_float(w.x);
+      v[4 * j + 1] = __uint_as_float(w.y);
+      v[4 * j + 2] = __uint_as_float(w.z);
+      v[4 * j + 3] = __uint_as_float(w.w);
+    }
+  } else {
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) + off);
+    uint4 w[E / 8];
+#pragma unroll
+    for (int j = 0; j < E / 8; ++j) w[j] = __ldg(p + j);
+#pragma unroll
+    for (int j = 0; j < E / 8; ++j) {
+      Raw8 r;
+      r.a = w[j];
+      float f[8];
+      unpack_raw<DT>(r, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[8 * j + i] = f[i];
+    }
+  }
+}
+
+__device__ __forceinline__ uint32_t code_markstein(float v, float s, float r) {
+  const float y = __fmul_rn(v, r);
+  const float e = __fmaf_rn(-s, y, v);       // exact residual
+  const float z = __fmaf_rn(e, r, y);        // RN(v / s)
+  return __float_as_uint(__fadd_rn(z, 12582912.0f));  // low byte = rint(z), |z| <= 127
+}
+
+template <int DT, int E = kLaneE>
+__global__ void __launch_bounds__(kLaneThreads, 1)
+    act_quant_lane_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int tpr, int rows_per_cta,
+                          int block, float inv, uint8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale) {
+  __shared__ uint32_t s_max[3][kLaneThreads];
+  const int tid = threadIdx.x;
+  const int r_local = tid / tpr;
+  const int part = tid - r_local * tpr;
+  const bool active = r_local < rows_per_cta;
+  const int lane = tid & 31;
+  const int64_t row_step = static_cast<int64_t>(gridDim.x) * rows_per_cta;
+  for (int i = tid; i < 3 * kLaneThreads; i += blockDim.x) (&s_max[0][0])[i] = 0u;
+  // 16-bit rows with E = 64: the next row group's slice (32 registers) is in
+  // flight while the current one is rotated and quantized.
+  constexpr bool kPrefetch = DT != kF32 && E == 64;
+  uint4 raw[kPrefetch ? E / 8 : 1];
+  auto issue = [&](int64_t b) {
+    const int64_t rw = b + r_local;
+    const bool lv = active && rw < M;
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(x) +
+                                                    (lv ? rw * ldx + static_cast<int64_t>(part) * E : 0));
+#pragma unroll
+    for (int j = 0; j < (kPrefetch ? E / 8 : 1); ++j) raw[j] = lv ? __ldg(p + j) : make_uint4(0u, 0u, 0u, 0u);
+  };
+  if constexpr (kPrefetch) issue(static_cast<int64_t>(blockIdx.x) * rows_per_cta);
+  __syncthreads();
+  int it = 0;
+  for (int64_t base = static_cast<int64_t>(blockIdx.x) * rows_per_cta; base < M; base += row_step, ++it) {
+    const int64_t row = base + r_local;
+    const bool live = active && row < M;
+    float v[E];
+    if constexpr (kPrefetch) {
+#pragma unroll
+      for (int j = 0; j < E / 8; ++j) {
+        Raw8 r8;
+        r8.a = raw[j];
+        float f[8];
+        unpack_raw<DT>(r8, f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[8 * j + i] = f[i];
+      }
+      if (base + row_step < M) issue(base + row_step);
+    } else {
+      load_slice<DT, E>(x, live ? row * ldx + static_cast<int64_t>(part) * E : 0, live, v);
+    }
+
+    if (block > 1) {
+#pragma unroll
+      for (int h = 1; h < E; h <<= 1) {
+        if (block > h) {
+#pragma unroll
+          for (int i = 0; i < E; ++i)
+            if (!(i & h)) {
+              const float a = v[i], b = v[i + h];
+              v[i] = __fadd_rn(a, b);
+              v[i + h] = __fsub_rn(a, b);
+            }
+        }
+      }
+      // stages h = E .. block/2: partner lane (h / E) away (same warp: the
+      // lanes of one block are consecutive and aligned); lower lane a + b,
+      // upper lane a - b with a the lower lane's value.
+      for (int d = 1; d * E < block; d <<= 1) {
+        const float sgn = (lane & d) ? -1.0f : 1.0f;
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+          const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
+          v[i] = __fmaf_rn(sgn, v[i], o);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], inv);
+    }
+
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const int sb = it % 3;
+    if (live) atomicMax(&s_max[sb][r_local], __float_as_uint(amax));
+    for (int i = tid; i < rows_per_cta; i += blockDim.x) s_max[(it + 1) % 3][i] = 0u;  // next iteration's
+    __syncthreads();
+    if (!live) continue;
+    amax = __uint_as_float(s_max[sb][r_local]);
+    float sc = __fdiv_rn(amax, 127.0f);
+    if (!(sc > 0.0f)) sc = 1.0f;
+
+    uint8_t* dst = q + row * ldq + static_cast<int64_t>(part) * E;
+    // Normal, finite scales: |RN(v/s)| <= 127 with no clamp needed, since
+    // s = RN(absmax/127) carries a relative error below 2^-24.  Subnormal
+    // scales lose that precision (quotients can exceed 127.5) and take the
+    // clamped IEEE division, like non-finite ones.
+    const bool exact_path = sc >= 1.1754943508222875e-38f && sc <= 3.4028234663852886e38f;
+    if (exact_path) {
+      float s2 = sc;
+      if (sc < 8.673617379884035e-19f) {         // 2^-60
+        s2 = __fmul_rn(sc, 1.8446744073709552e19f);  // x 2^64, exact
+#pragma unroll
+        for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], 1.8446744073709552e19f);
+      } else if (sc > 1.152921504606847e18f) {   // 2^60
+        s2 = __fmul_rn(sc, 5.421010862427522e-20f);  // x 2^-64, exact for s
+#pragma unroll
+        for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], 5.421010862427522e-20f);
+      }
+      const float r = __frcp_rn(s2);
+#pragma unroll
+      for (int j = 0; j < E / 16; ++j) {
+        uint32_t w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t c0 = code_markstein(v[16 * j + 4 * t], s2, r);
+          const uint32_t c1 = code_markstein(v[16 * j + 4 * t + 1], s2, r);
+          const uint32_t c2 = code_markstein(v[16 * j + 4 * t + 2], s2, r);
+          const uint32_t c3 = code_markstein(v[16 * j + 4 * t + 3], s2, r);
+          w[t] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+        }
+        *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < E / 16; ++j) {
+        uint32_t w[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t c0 = slow_int8(v[16 * j + 4 * t], sc);
+          const uint32_t c1 = slow_int8(v[16 * j + 4 * t + 1], sc);
+          const uint32_t c2 = slow_int8(v[16 * j + 4 * t + 2], sc);
+          const uint32_t c3 = slow_int8(v[16 * j + 4 * t + 3], sc);
+          w[t] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+        }
+        *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    if (part == 0) scale[row] = sc;
+  }
+}
+
+// 0 automatic (the lane-block kernel where it applies, else the warp-shuffle
+// kernel), 1 warp-shuffle kernel, 2 lane-block kernel (a verification and
+// tuning knob).
+static int g_prologue_path = 0;
+void set_prologue_path(int path) { g_prologue_path = path; }
+
+// Small CTAs (about 128 threads: whole rows of TPR lanes), several per SM,
+// so that one CTA's loads overlap another's arithmetic across the per-row
+// barrier.
+template <int DT>
+static cudaError_t launch_lane(int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K, int block,
+                               float inv, uint8_t* q, int64_t ldq, float* scale) {
+  auto kernel = act_quant_lane_kernel<DT>;
+  const int tpr = K / kLaneE;
+  int rows = 128 / tpr;
+  if (rows < 1) rows = 1;
+  const int threads = (rows * tpr + 31) / 32 * 32;
+  static int per_sm[64][8] = {{0}};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int slot = threads / 32 - 1;  // 1..12 warps -> slot 0..11; cache the common ones
+  int n = 0;
+  if (dev < 64 && slot < 8 && per_sm[dev][slot] > 0) {
+    n = per_sm[dev][slot];
+  } else {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess || n <= 0) n = 1;
+    if (dev < 64 && slot < 8) per_sm[dev][slot] = n;
+  }
+  const int64_t need = (M + rows - 1) / rows;
+  const int64_t cap = static_cast<int64_t>(device_sm_count()) * n;
+  const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
+  kernel<<<grid, threads, 0, st>>>(x, ldx, static_cast<int>(M), K, tpr, rows, block, inv, q, ldq, scale);
+  return cudaGetLastError();
+}
+
+// The lane-block kernel applies to INT8 ties-to-even codes of 16/32-bit
+// inputs whose rows split into whole 64-element slices (at most
+// kLaneThreads), with 16-byte aligned input and code rows and rotation
+// blocks of at most 32 lanes.
+static bool lane_ok(int x_dtype, int quant, int64_t K, int block, bool vin16, bool vout16) {
+  if (quant != 0 || !(x_dtype == kF16 || x_dtype == kBF16 || x_dtype == kF32)) return false;
+  if (!vin16 || !vout16 || K % kLaneE != 0 || K / kLaneE > kLaneThreads) return false;
+  return block <= 1 || block <= 32 * kLaneE;
+}
+
 template <int DT, int SPW, int QUANT>
 static cudaError_t launch_one(int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K, int wpr,
                               int block, float inv, uint8_t* q, int64_t ldq, float* scale, int vin,
@@ -343,9 +595,23 @@ static bool choose_layout(int64_t K, int block, int* wpr, int* spw) {
 cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
                           int quant, void* q, int64_t ldq, float* scale, cudaStream_t stream) {
   if (M == 0) return cudaSuccess;
+  const int eb = x_dtype == kF32 ? 4 : (x_dtype == kE4M3 || x_dtype == kE5M2) ? 1 : 2;
+  const float inv_b = block > 1 ? static_cast<float>(1.0 / sqrt(static_cast<double>(block))) : 1.0f;
+  {
+    const bool vin16 = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ldx * eb) % 16 == 0);
+    const bool vout16 = (reinterpret_cast<uintptr_t>(q) % 16 == 0) && (ldq % 16 == 0);
+    if (g_prologue_path != 1 && lane_ok(x_dtype, quant, K, block, vin16, vout16)) {
+      uint8_t* qb = static_cast<uint8_t*>(q);
+      const int k = static_cast<int>(K);
+      switch (x_dtype) {
+        case kF32: return launch_lane<kF32>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale);
+        case kF16: return launch_lane<kF16>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale);
+        default: return launch_lane<kBF16>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale);
+      }
+    }
+  }
   int wpr = 1, spw = 1;
   if (!choose_layout(K, block, &wpr, &spw)) return cudaErrorInvalidValue;
-  const int eb = x_dtype == kF32 ? 4 : (x_dtype == kE4M3 || x_dtype == kE5M2) ? 1 : 2;
   const int vin = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((ldx * eb) % 16 == 0);
   const int vout = (reinterpret_cast<uintptr_t>(q) % 8 == 0) && (ldq % 8 == 0);
   const float inv = block > 1 ? static_cast<float>(1.0 / sqrt(static_cast<double>(block))) : 1.0f;

@@ -42,6 +42,16 @@ def set_gemm_path(path):
     nat.check(nat.library().b2_set_gemm_path(code), "b2_set_gemm_path")
 
 
+def set_prologue_path(path):
+    """Process-wide activation-prologue kernel: "auto", "shuffle" (warp
+    shuffle butterflies, every quantizer) or "lane" (one lane per 64
+    elements, INT8 ties-to-even codes of 16-byte aligned rows; other calls
+    fall back to "shuffle").  Codes and scales are bit-identical; this is a
+    tuning and verification knob."""
+    code = {"auto": 0, "shuffle": 1, "lane": 2}[path]
+    nat.check(nat.library().b2_set_prologue_path(code), "b2_set_prologue_path")
+
+
 def _round_up(v, m):
     return (v + m - 1) // m * m
 

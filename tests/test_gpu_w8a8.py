@@ -120,11 +120,18 @@ def test_int8_gemm_dequant_epilogues(rounding, out_dtype, scalar, gemm_path):
 
 
 # ----------------------------------------------------- prologue (act_quant)
+@pytest.fixture(params=["shuffle", "lane"])
+def prologue_path(request):
+    qlinear.set_prologue_path(request.param)
+    yield request.param
+    qlinear.set_prologue_path("auto")
+
+
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("k,block", [(3072, 128), (3072, None), (3072, 256), (3072, 1024),
                                      (384, 128), (4096, 128), (5120, 128), (12288, 128),
                                      (8192, 2048), (16384, 256), (80, 16), (24, None)])
-def test_act_quant_bit_exact(dtype, k, block):
+def test_act_quant_bit_exact(dtype, k, block, prologue_path):
     rng = np.random.default_rng(k + (block or 0))
     m = 67
     x32 = outlier_activations(rng, m, k)
@@ -137,10 +144,11 @@ def test_act_quant_bit_exact(dtype, k, block):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_act_quant_exact_ties_round_to_even(dtype):
-    """Rows whose scale is exactly 1 (absmax 127) with values on x.5: the
-    fast quantizer must defer to the exact division and round ties to even,
-    like the oracle (k = 1024 runs the wide-lane kernel)."""
+def test_act_quant_exact_ties_round_to_even(dtype, prologue_path):
+    """Rows whose scale is exactly 1 (absmax 127) with values on x.5: both
+    kernels' quantizers (the shuffle kernel's fast path with its exact
+    fallback, the lane kernel's FMA-corrected quotient) must round ties to
+    even, like the oracle."""
     k = 1024
     x32 = np.zeros((4, k), dtype=np.float32)
     ties = np.array([0.5, 1.5, 2.5, 3.5, -0.5, -1.5, -2.5, 126.5, -126.5, 64.5], dtype=np.float32)
@@ -153,6 +161,28 @@ def test_act_quant_exact_ties_round_to_even(dtype):
     assert np.array_equal(s.cpu().numpy().view(np.uint32), ref_s.view(np.uint32))
     assert np.array_equal(q.cpu().numpy(), ref_q)
     assert list(q.cpu().numpy()[0, 1:5]) == [0, 2, 2, 4]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("block", [None, 128])
+def test_act_quant_extreme_scales(dtype, block, prologue_path):
+    """Row scales far from 1: below 2^-60 and above 2^60 (the lane kernel's
+    exact power-of-two rescaling), subnormal (clamped IEEE division), and
+    rows of exact ties at scale 1, against the oracle's IEEE division."""
+    rng = np.random.default_rng(11)
+    x32 = outlier_activations(rng, 9, 3072)
+    x32[0] *= 1e-25
+    x32[1] *= 1e-39
+    x32[2] *= 1e30
+    x32[3] *= 7e-20
+    x32[4] *= 3e19
+    x32[5] *= 1e-44 if dtype == torch.float32 else 1e-40
+    x32[6] = np.round(x32[6] * 2.0) / 2.0
+    xt = x_tensor(x32, dtype)
+    q, s = rdna2_ops.act_quant(xt, rotation_block=block)
+    ref_q, ref_s = oracle.act_quant_int8(x_bits(xt), ODT[dtype], block or 0)
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), ref_s.view(np.uint32))
+    assert np.array_equal(q.cpu().numpy(), ref_q)
 
 
 def test_act_quant_e4m3_bit_exact():
