@@ -547,7 +547,7 @@ def run_workload(args):
                                           lambda x, w: rdna2_ops.fp8_linear(x, w, sw, out_dtype=torch.bfloat16))
         metric, flops, launches = f"FP8 e4m3 linear TFLOPS (config 4, M={m})", 2.0 * m * n * k, 2
         traffic = n * k + n * 4 + m * k * 2 + m * n * 2
-        if m == 1:
+        if m <= 32:  # decode sizes stream the weights: HBM-bound
             bound, peak, unit = "hbm", pk["hbm_gbs"], "GB/s"
         else:
             bound, peak, unit = "tensor", 2.0 * pk["bf16_tflops"], "TFLOP/s"

@@ -54,8 +54,11 @@ int b2_pair_capacity(void);
  * with automatic N tile), 3 = single N=256, 4 = single N=128, 5 = pair
  * N=256, 6 = pair N=192, 7 = pair N=256 with the output staged in shared
  * memory and written by TMA stores (automatic choice for pair tiles whose
- * output rows are 16-byte aligned; 5 otherwise).  A tuning and verification
- * knob; results are identical for every choice.
+ * output rows are 16-byte aligned; 5 otherwise), 8 = split-K: M <= 32 only
+ * (automatic there), 128-row swap-AB weight tiles split along K over the
+ * CTAs of a thread-block cluster and reduced in the leader's shared memory.
+ * A tuning and verification knob; INT8 results are identical for every
+ * choice, floating kinds differ only in fp32 summation order.
  * No reference counterpart (the reference exposes tile keywords instead,
  * rdna2_ops/int8_gemm.py:195-214). */
 int b2_set_gemm_path(int path);

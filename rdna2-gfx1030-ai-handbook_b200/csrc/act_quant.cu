@@ -170,8 +170,9 @@ template <int DT, int SPW, int QUANT>
 __global__ void __launch_bounds__(128)
     act_quant_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int wpr, int block,
                      float inv, uint8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale,
-                     int vec_in, int vec_out) {
+                     int vec_in, int vec_out, int early) {
   __shared__ float s_max[2][4];
+  if (early) griddep_launch_dependents();  // the GEMM may set up while the codes are written
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int groups = 4 / wpr;
   const int g = warp / wpr, part = warp % wpr;
@@ -359,8 +360,10 @@ __device__ __forceinline__ uint32_t code_markstein(float v, float s, float r) {
 template <int DT, int E = kLaneE>
 __global__ void __launch_bounds__(kLaneThreads, 1)
     act_quant_lane_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int tpr, int rows_per_cta,
-                          int block, float inv, uint8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale) {
+                          int block, float inv, uint8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale,
+                          int early) {
   __shared__ uint32_t s_max[3][kLaneThreads];
+  if (early) griddep_launch_dependents();  // the GEMM may set up while the codes are written
   const int tid = threadIdx.x;
   const int r_local = tid / tpr;
   const int part = tid - r_local * tpr;
@@ -503,7 +506,7 @@ void set_prologue_path(int path) { g_prologue_path = path; }
 // barrier.
 template <int DT>
 static cudaError_t launch_lane(int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K, int block,
-                               float inv, uint8_t* q, int64_t ldq, float* scale) {
+                               float inv, uint8_t* q, int64_t ldq, float* scale, int early) {
   auto kernel = act_quant_lane_kernel<DT>;
   const int tpr = K / kLaneE;
   int rows = 128 / tpr;
@@ -523,7 +526,7 @@ static cudaError_t launch_lane(int64_t M, cudaStream_t st, const void* x, int64_
   const int64_t need = (M + rows - 1) / rows;
   const int64_t cap = static_cast<int64_t>(device_sm_count()) * n;
   const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
-  kernel<<<grid, threads, 0, st>>>(x, ldx, static_cast<int>(M), K, tpr, rows, block, inv, q, ldq, scale);
+  kernel<<<grid, threads, 0, st>>>(x, ldx, static_cast<int>(M), K, tpr, rows, block, inv, q, ldq, scale, early);
   return cudaGetLastError();
 }
 
@@ -538,7 +541,7 @@ static bool lane_ok(int x_dtype, int quant, int64_t K, int block, bool vin16, bo
 }
 
 template <int DT, int SPW, int QUANT>
-static cudaError_t launch_one(int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K, int wpr,
+static cudaError_t launch_one(int early, int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K, int wpr,
                               int block, float inv, uint8_t* q, int64_t ldq, float* scale, int vin,
                               int vout) {
   auto kernel = act_quant_kernel<DT, SPW, QUANT>;
@@ -554,18 +557,18 @@ static cudaError_t launch_one(int64_t M, cudaStream_t st, const void* x, int64_t
   const int64_t need = (M + groups - 1) / groups;
   const int64_t cap = static_cast<int64_t>(device_sm_count()) * (dev < 64 ? per_sm[dev] : 4);
   const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
-  kernel<<<grid, 128, 0, st>>>(x, ldx, static_cast<int>(M), K, wpr, block, inv, q, ldq, scale, vin,
-                               vout);
+  kernel<<<grid, 128, 0, st>>>(x, ldx, static_cast<int>(M), K, wpr, block, inv, q, ldq, scale, vin, vout,
+                               early);
   return cudaGetLastError();
 }
 
 template <int DT, int QUANT>
-static cudaError_t launch_spw(int spw, int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K,
+static cudaError_t launch_spw(int early, int spw, int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K,
                              int wpr, int block, float inv, uint8_t* q, int64_t ldq, float* scale,
                              int vin, int vout) {
 #define B2_SPW_CASE(S) \
   case S:              \
-    return launch_one<DT, S, QUANT>(M, st, x, ldx, K, wpr, block, inv, q, ldq, scale, vin, vout);
+    return launch_one<DT, S, QUANT>(early, M, st, x, ldx, K, wpr, block, inv, q, ldq, scale, vin, vout);
   switch (spw) {
     B2_SPW_CASE(1) B2_SPW_CASE(2) B2_SPW_CASE(3) B2_SPW_CASE(4) B2_SPW_CASE(5) B2_SPW_CASE(6)
     B2_SPW_CASE(7) B2_SPW_CASE(8) B2_SPW_CASE(10) B2_SPW_CASE(12) B2_SPW_CASE(16)
@@ -593,8 +596,10 @@ static bool choose_layout(int64_t K, int block, int* wpr, int* spw) {
 }
 
 cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
-                          int quant, void* q, int64_t ldq, float* scale, cudaStream_t stream) {
+                          int quant, void* q, int64_t ldq, float* scale, cudaStream_t stream,
+                          bool early_dependents) {
   if (M == 0) return cudaSuccess;
+  const int early = early_dependents ? 1 : 0;
   const int eb = x_dtype == kF32 ? 4 : (x_dtype == kE4M3 || x_dtype == kE5M2) ? 1 : 2;
   const float inv_b = block > 1 ? static_cast<float>(1.0 / sqrt(static_cast<double>(block))) : 1.0f;
   {
@@ -604,9 +609,9 @@ cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int6
       uint8_t* qb = static_cast<uint8_t*>(q);
       const int k = static_cast<int>(K);
       switch (x_dtype) {
-        case kF32: return launch_lane<kF32>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale);
-        case kF16: return launch_lane<kF16>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale);
-        default: return launch_lane<kBF16>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale);
+        case kF32: return launch_lane<kF32>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
+        case kF16: return launch_lane<kF16>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
+        default: return launch_lane<kBF16>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
       }
     }
   }
@@ -617,7 +622,8 @@ cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   const float inv = block > 1 ? static_cast<float>(1.0 / sqrt(static_cast<double>(block))) : 1.0f;
   uint8_t* qb = static_cast<uint8_t*>(q);
   const int k = static_cast<int>(K);
-#define B2_AQ(DT, Q) return launch_spw<DT, Q>(spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout)
+#define B2_AQ(DT, Q) \
+  return launch_spw<DT, Q>(early, spw, M, stream, x, ldx, k, wpr, block, inv, qb, ldq, scale, vin, vout)
 #define B2_AQ_DT(Q)                 \
   switch (x_dtype) {                \
     case kF32: B2_AQ(kF32, Q);      \

@@ -108,6 +108,18 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// ------------------------------------------ programmatic dependent launch
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel in the stream still runs (once that kernel has called
+// griddep_launch_dependents, or at its exit otherwise); griddep_wait blocks
+// until the previous kernel has completed and its memory is visible.  Work
+// that does not read the previous kernel's results (weights, barriers, TMEM)
+// goes before the wait.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------ clusters
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

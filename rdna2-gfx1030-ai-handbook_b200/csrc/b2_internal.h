@@ -39,9 +39,13 @@ int pair_capacity();
 
 // Per-row rotate + quantize (quant 0 = int8 /127 RNE, 1 = e4m3 /448, 2 = the
 // reference row quantizer: int8, half away from zero, step floor 1e-20).
+// early_dependents: let the next kernel in the stream (the fused linear's
+// GEMM, launched with programmatic serialization) start its setup and
+// weight loads while this one runs; only for callers whose next kernel reads
+// nothing else this kernel's predecessors may still write.
 cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                           int block, int quant, void* q, int64_t ldq, float* scale,
-                          cudaStream_t stream);
+                          cudaStream_t stream, bool early_dependents = false);
 
 cudaError_t run_fp8_decode(const void* w, int fp8_dtype, int64_t rows, int64_t cols, int64_t ld,
                            int out_dtype, void* out, int64_t ldo, cudaStream_t stream);

@@ -85,7 +85,7 @@ int b2_sm_count(void) { return b2::device_sm_count(); }
 int b2_pair_capacity(void) { return b2::pair_capacity(); }
 
 int b2_set_gemm_path(int path) {
-  if (path < 0 || path > 7) return fail();
+  if (path < 0 || path > 8) return fail();
   b2::set_gemm_path(path);
   return 0;
 }
@@ -153,7 +153,7 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
   float* sa = reinterpret_cast<float*>(q + round_up(M * ldq, 256));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = b2::run_act_quant(x, x_dtype, M, K, ldx, block, kind == b2::kKindE4M3 ? 1 : 0, q,
-                                    ldq, sa, s);
+                                    ldq, sa, s, /*early_dependents=*/true);
   if (e != cudaSuccess) return static_cast<int>(e);
   b2::GemmParams p = make_params(M, N, K, sa, w_scale, w_scale_count, bias, bias_dtype, epilogue,
                                  out, out_dtype, ldc);

@@ -438,6 +438,7 @@ __global__ void __launch_bounds__(192, 1)
     // Producer.  The whole warp runs the loop and one elected lane issues:
     // a loop run by a single lane of a diverged warp pays a large
     // per-iteration cost on this part.
+    griddep_wait();  // operands may come from the previous kernel
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
@@ -511,6 +512,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int quarter = warp & 3;  // TMEM lanes this warp may access
     float* wsb = reinterpret_cast<float*>(smem + L::kOffEpi) + (warp - 2) * 64;
+    griddep_wait();
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
       const int buf = t & 1;
@@ -599,6 +601,7 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     // Producer (whole warp loops, one elected lane issues).
+    griddep_wait();  // operands may come from the previous kernel
     const uint32_t full_leader = mapa_shared(smem_u32(&full[0]), 0);
     int stage = 0;
     uint32_t phase = 0;
@@ -681,6 +684,7 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t tempty_leader = mapa_shared(smem_u32(&tempty[0]), 0);
     const uint32_t obuf = smem_u32(smem + L::kOffOut) + static_cast<uint32_t>((warp - 2) * 2 * kOutBufBytes);
     uint32_t ob_sel = 0;
+    griddep_wait();
     int t = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++t) {
       const int buf = t & 1;
@@ -716,6 +720,261 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, L::kTmemCols);
+  }
+}
+
+// ------------------------------------------------ split-K kernel (M <= 32)
+// Decode-sized problems (M <= 32 tokens) are weight-streaming bound: with
+// 128 x BN output tiles only ceil(N/128) SMs would read the weights.  Here
+// the weight tile is the 128-row A operand and the tokens the N = BT
+// operand (swap-AB), and each 128-row tile is split along K over the S CTAs
+// of one thread-block cluster (S <= 8, S * tiles <= SMs).  Every CTA streams
+// its contiguous k-block range through a TMA ring into its own TMEM
+// accumulator; the S-1 non-leader CTAs then write their accumulators into
+// the leader's shared memory over distributed shared memory, and after one
+// cluster barrier the leader adds them in rank order (exact for int32,
+// a fixed order for fp32) and runs the epilogue.  No global workspace, no
+// inter-CTA spin waits.
+constexpr int kSplitMax = 8;
+
+template <int BT, int STAGES>
+struct SplitSmem {
+  static constexpr int kWBytes = 128 * 128;
+  static constexpr int kXBytes = BT * 128;
+  static constexpr int kStageBytes = kWBytes + kXBytes;
+  static constexpr int kOffW = 0;
+  static constexpr int kOffX = STAGES * kWBytes;
+  static constexpr int kOffPart = kOffX + STAGES * kXBytes;              // [S-1][128][BT] 32-bit
+  static constexpr int kOffBar = kOffPart + (kSplitMax - 1) * 128 * BT * 4;
+  static constexpr int kOffMisc = kOffBar + (2 * STAGES + 1) * 8;
+  static constexpr int kBytes = kOffMisc + 16;
+  static constexpr int kAlloc = kBytes + 1024;
+  static_assert(kXBytes % 1024 == 0, "swizzle atoms need 1 KiB alignment");
+  static_assert(kAlloc <= 232448, "shared memory budget");
+};
+
+template <int KIND, int MODE, int OUT, int BT>
+__device__ __forceinline__ void splitk_store(const GemmParams& p, const uint32_t (&v)[BT], int n) {
+  if (n >= p.N) return;
+  float sb = 0.0f, b = 0.0f;
+  load_col(p, n, (p.sb != nullptr && p.sb_scalar) ? p.sb[0] : 0.0f, sb, b);
+  const bool hb = p.bias != nullptr;
+  const int mt = p.M < BT ? p.M : BT;
+#pragma unroll
+  for (int t = 0; t < BT; ++t) {
+    if (t >= mt) break;
+    float y;
+    if constexpr (MODE == kEpiNone) {
+      y = __uint_as_float(v[t]);
+    } else {
+      y = epi_value<KIND, MODE, OUT>(v[t], p.sa[t], sb, b, hb);
+    }
+    const int64_t o = static_cast<int64_t>(t) * p.ldc + n;
+    if constexpr (OUT == kF32 || OUT == kI32) {
+      static_cast<uint32_t*>(p.out)[o] = __float_as_uint(y);
+    } else if constexpr (OUT == kF16) {
+      static_cast<__half*>(p.out)[o] = __float2half_rn(y);
+    } else {
+      static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(y);
+    }
+  }
+}
+
+template <int KIND, int BT>
+__device__ __forceinline__ void splitk_store_dispatch(const GemmParams& p, const uint32_t (&v)[BT], int n) {
+  switch (p.epilogue * 4 + p.out_dtype) {
+    case kEpiNone * 4 + kI32: splitk_store<KIND, kEpiNone, kI32, BT>(p, v, n); break;
+    case kEpiSeparate * 4 + kF32: splitk_store<KIND, kEpiSeparate, kF32, BT>(p, v, n); break;
+    case kEpiSeparate * 4 + kF16: splitk_store<KIND, kEpiSeparate, kF16, BT>(p, v, n); break;
+    case kEpiSeparate * 4 + kBF16: splitk_store<KIND, kEpiSeparate, kBF16, BT>(p, v, n); break;
+    case kEpiFma * 4 + kF32: splitk_store<KIND, kEpiFma, kF32, BT>(p, v, n); break;
+    case kEpiFma * 4 + kF16: splitk_store<KIND, kEpiFma, kF16, BT>(p, v, n); break;
+    case kEpiFma * 4 + kBF16: splitk_store<KIND, kEpiFma, kBF16, BT>(p, v, n); break;
+    case kEpiKitchen * 4 + kF32: splitk_store<KIND, kEpiKitchen, kF32, BT>(p, v, n); break;
+    case kEpiKitchen * 4 + kF16: splitk_store<KIND, kEpiKitchen, kF16, BT>(p, v, n); break;
+    case kEpiKitchen * 4 + kBF16: splitk_store<KIND, kEpiKitchen, kBF16, BT>(p, v, n); break;
+    default: break;
+  }
+}
+
+template <int KIND, int BT, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    qgemm_splitk_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_x,
+                        const GemmParams p) {
+  using L = SplitSmem<BT, STAGES>;
+  constexpr int kKbElems = (KIND == kKindBF16 || KIND == kKindF16) ? 64 : 128;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = static_cast<int>(cluster_ctarank());
+  const int splits = static_cast<int>(gridDim.x) / p.tiles_m;  // cluster size
+  const int tile = static_cast<int>(cluster_id_x());
+  const int kb0 = static_cast<int>((static_cast<int64_t>(rank) * p.num_kb) / splits);
+  const int kb1 = static_cast<int>((static_cast<int64_t>(rank + 1) * p.num_kb) / splits);
+  constexpr uint32_t kTmemCols = tmem_cols_for(BT);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tma_w);
+    tma_prefetch_desc(&tma_x);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  cluster_sync();  // every CTA of the cluster running, barriers and TMEM ready
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // The weights do not depend on the previous kernel (the activation
+    // prologue): the first ring's worth streams in before the wait.
+    const int pre = kb1 - kb0 < STAGES ? kb1 - kb0 : STAGES;
+    if (elect_one()) {
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], L::kStageBytes);
+        tma_load_2d(&tma_w, &full[i], smem + L::kOffW + i * L::kWBytes, (kb0 + i) * kKbElems, tile * 128);
+      }
+    }
+    __syncwarp();
+    griddep_wait();
+    if (elect_one()) {
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(&tma_x, &full[i], smem + L::kOffX + i * L::kXBytes, (kb0 + i) * kKbElems, 0);
+    }
+    __syncwarp();
+    int stage = pre == STAGES ? 0 : pre;
+    uint32_t phase = pre == STAGES ? 1u : 0u;
+    bool ok = true;
+    for (int kb = kb0 + pre; kb < kb1 && ok; ++kb) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status));
+      if (!ok) break;
+      if (elect_one()) {
+        mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+        tma_load_2d(&tma_w, &full[stage], smem + L::kOffW + stage * L::kWBytes, kb * kKbElems, tile * 128);
+        tma_load_2d(&tma_x, &full[stage], smem + L::kOffX + stage * L::kXBytes, kb * kKbElems, 0);
+      }
+      __syncwarp();
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    for (int i = 0; i < STAGES && ok; ++i) {  // every slot released before exit
+      ok = __all_sync(0xffffffffu, mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kSiteProducer, p.status));
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  } else if (warp == 1) {
+    constexpr uint32_t idesc = make_idesc<KIND>(128, BT);
+    const uint64_t w_desc0 = sw128_desc(smem_u32(smem + L::kOffW));
+    const uint64_t x_desc0 = sw128_desc(smem_u32(smem + L::kOffX));
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int kb = kb0; kb < kb1 && ok; ++kb) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort_flag, kSiteMma, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      if (elect_one()) {
+        const uint64_t wd = w_desc0 + static_cast<uint32_t>((stage * L::kWBytes) >> 4);
+        const uint64_t xd = x_desc0 + static_cast<uint32_t>((stage * L::kXBytes) >> 4);
+        umma<KIND>(tmem_base, wd, xd, idesc, kb != kb0 ? 1u : 0u);
+        umma<KIND>(tmem_base, wd + 2, xd + 2, idesc, 1u);
+        umma<KIND>(tmem_base, wd + 4, xd + 4, idesc, 1u);
+        umma<KIND>(tmem_base, wd + 6, xd + 6, idesc, 1u);
+        umma_commit(&empty[stage]);
+      }
+      __syncwarp();
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    // the accumulator is complete (or, for an empty k range, stays unread)
+    if (elect_one()) umma_commit(acc_full);
+    __syncwarp();
+  }
+
+  // Epilogue warps 2..5: TMEM lane = weight row (tile * 128 + q * 32 + lane),
+  // columns = tokens.
+  const int quarter = warp & 3;
+  const int row_local = quarter * 32 + lane;
+  const bool epi = warp >= 2;
+  uint32_t v[BT];
+  bool have = false;
+  if (epi) griddep_wait();  // scales may come from the previous kernel
+  if (epi && kb1 > kb0) {
+    have = mbar_wait(acc_full, 0, abort_flag, kSiteEpilogue, p.status);
+    have = __all_sync(0xffffffffu, have);
+    if (have) {
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      if constexpr (BT == 16) {
+        tmem_ld16(taddr, v);
+        tmem_ld_wait16(v);
+      } else {
+        tmem_ld32(taddr, v);
+        tmem_ld_wait(v);
+      }
+    }
+  }
+  if (!have) {
+#pragma unroll
+    for (int t = 0; t < BT; ++t) v[t] = 0u;
+  }
+  if (epi && rank > 0) {
+    // this CTA's partial sums -> the leader's [rank-1][row][BT] slot
+    const uint32_t dst = mapa_shared(smem_u32(smem + L::kOffPart), 0) +
+                         static_cast<uint32_t>(((rank - 1) * 128 + row_local) * BT * 4);
+#pragma unroll
+    for (int t = 0; t < BT; t += 4)
+      asm volatile("st.shared::cluster.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst + t * 4), "r"(v[t]),
+                   "r"(v[t + 1]), "r"(v[t + 2]), "r"(v[t + 3])
+                   : "memory");
+  }
+  tc_fence_before();
+  cluster_sync();  // partials visible in the leader; no CTA touches TMEM after this
+  if (epi && rank == 0) {
+    const uint32_t part = smem_u32(smem + L::kOffPart) + static_cast<uint32_t>(row_local * BT * 4);
+    for (int r = 1; r < splits; ++r) {
+      const uint32_t src = part + static_cast<uint32_t>((r - 1) * 128 * BT * 4);
+#pragma unroll
+      for (int t = 0; t < BT; t += 4) {
+        const uint4 w = lds_v4(src + t * 4);
+        const uint32_t o[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          if constexpr (KIND == kKindI8) {
+            v[t + i] = static_cast<uint32_t>(static_cast<int>(v[t + i]) + static_cast<int>(o[i]));
+          } else {
+            v[t + i] = __float_as_uint(__fadd_rn(__uint_as_float(v[t + i]), __uint_as_float(o[i])));
+          }
+        }
+      }
+    }
+    splitk_store_dispatch<KIND, BT>(p, v, tile * 128 + row_local);
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -823,8 +1082,18 @@ static cudaError_t launch_single(const void* a, int64_t lda, const void* b, int6
   int grid = device_sm_count();
   if (max_ctas > 0 && max_ctas < grid) grid = max_ctas;
   if (tiles < grid) grid = tiles;
-  kernel<<<grid, 192, L::kAlloc, stream>>>(ma, mb, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddep_wait
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 template <int KIND, int BN, int STAGES, bool TSTORE>
@@ -838,11 +1107,13 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
   if (e != cudaSuccess) return e;
   const int dev = current_device();
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddep_wait
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = L::kAlloc;
   cfg.stream = stream;
@@ -876,7 +1147,64 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
   if (max_ctas > 0 && max_ctas / 2 < pairs) pairs = max_ctas / 2 > 0 ? max_ctas / 2 : 1;
   if (tiles < pairs) pairs = tiles;
   cfg.gridDim = dim3(2 * pairs);
+  cfg.numAttrs = 2;
   e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, p);
+  return e != cudaSuccess ? e : cudaGetLastError();
+}
+
+template <int KIND, int BT, int STAGES>
+static cudaError_t launch_splitk(const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams p,
+                                 cudaStream_t stream) {
+  using L = SplitSmem<BT, STAGES>;
+  auto kernel = qgemm_splitk_kernel<KIND, BT, STAGES>;
+  static bool configured[64] = {false};
+  static int active[64][kSplitMax + 1] = {{0}};
+  cudaError_t e = configure_once(kernel, L::kAlloc, configured);
+  if (e != cudaSuccess) return e;
+  const int dev = current_device();
+  const int T = static_cast<int>((p.N + 127) / 128);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // see griddep_wait
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = L::kAlloc;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  // The largest split whose T clusters are all co-resident (one wave), at
+  // most one CTA per k-block.
+  int splits = 1;
+  for (int s = kSplitMax; s >= 2; --s) {
+    if (s > p.num_kb || T * s > device_sm_count()) continue;
+    if (active[dev][s] == 0) {
+      attr[0].val.clusterDim.x = s;
+      cfg.gridDim = dim3(s * T);
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        n = -1;
+      }
+      active[dev][s] = n;
+    }
+    if (active[dev][s] >= T) {
+      splits = s;
+      break;
+    }
+  }
+  const int eb = (KIND == kKindBF16 || KIND == kKindF16) ? 2 : 1;
+  CUtensorMap mw, mx;
+  if ((e = make_kmajor_map(&mw, b, eb, p.K, p.N, ldb * eb, 128)) != cudaSuccess) return e;
+  if ((e = make_kmajor_map(&mx, a, eb, p.K, p.M, lda * eb, BT)) != cudaSuccess) return e;
+  p.tiles_m = T;
+  p.tiles_n = 1;
+  attr[0].val.clusterDim.x = splits;
+  cfg.gridDim = dim3(splits * T);
+  cfg.numAttrs = 2;
+  e = cudaLaunchKernelEx(&cfg, kernel, mw, mx, p);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
@@ -931,7 +1259,8 @@ static int choose_config(int64_t M, int64_t N) {
 
 // Kernel selection: 0 auto; 1 single-CTA (auto N tile); 2 pair (auto N tile);
 // 3 single BN=256; 4 single BN=128; 5 pair BN=256; 6 pair BN=192;
-// 7 pair BN=256 with the TMA-store epilogue (needs 16-byte aligned output rows).
+// 7 pair BN=256 with the TMA-store epilogue (needs 16-byte aligned output rows);
+// 8 split-K swap-AB cluster kernel (M <= 32 only).
 static int g_force_path = 0;
 
 template <int KIND>
@@ -946,6 +1275,9 @@ static cudaError_t dispatch(int cfg, const void* a, int64_t lda, const void* b, 
     case 6: return launch_pair<KIND, 192, 7, false>(a, lda, b, ldb, p, max_ctas, stream);
     // 6 stages + 32 KiB of output staging
     case 7: return launch_pair<KIND, 256, 6, true>(a, lda, b, ldb, p, max_ctas, stream);
+    case 8:
+      return p.M <= 16 ? launch_splitk<KIND, 16, 8>(a, lda, b, ldb, p, stream)
+                       : launch_splitk<KIND, 32, 5>(a, lda, b, ldb, p, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -960,6 +1292,8 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
   int cfg = g_force_path;
   const int64_t tm = (p.M + 127) / 128;
   const bool wide = p.N > 128 && tm * ((p.N + 255) / 256) >= device_sm_count() / 2;
+  if (cfg == 8 && p.M > 32) cfg = 0;  // split-K covers decode sizes only
+  if (cfg == 0 && p.M <= 32) cfg = 8;
   if (cfg == 0) {
     cfg = choose_config(p.M, p.N);
     // Staged TMA stores: whole 128-byte lines instead of 32 half-sector

@@ -47,7 +47,7 @@ def x_bits(xt):
     return bits(xt)
 
 
-@pytest.fixture(params=["single256", "single128", "pair256", "pair192", "pair256s"])
+@pytest.fixture(params=["single256", "single128", "pair256", "pair192", "pair256s", "splitk"])
 def gemm_path(request):
     qlinear.set_gemm_path(request.param)
     yield request.param
@@ -80,7 +80,7 @@ def test_int8_known_answer(golden, key, gemm_path):
 
 @pytest.mark.parametrize("m,n,k", [(1, 1, 1), (1, 16, 16), (37, 53, 79), (129, 257, 33),
                                    (128, 256, 128), (300, 200, 1000), (513, 640, 3072), (1024, 9472, 384),
-                                   (64, 96, 131071 // 8)])
+                                   (64, 96, 131071 // 8), (16, 5120, 640), (32, 300, 4096), (5, 20000, 256)])
 def test_int8_matmul_exact(m, n, k, gemm_path):
     rng = np.random.default_rng(m * 7 + n * 3 + k)
     a = rng.integers(-128, 128, (m, k), dtype=np.int8)
@@ -117,6 +117,71 @@ def test_int8_gemm_dequant_epilogues(rounding, out_dtype, scalar, gemm_path):
     out = rdna2_ops.int8_gemm_dequant(cuda(a), cuda(w).T, cuda(sa), cuda(sb), cuda(bias),
                                       rounding=rounding, out_dtype=out_dtype)
     assert same_bits(out, ref)
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 5120, 5120), (13, 1000, 640), (32, 4096, 1024), (3, 20000, 256)])
+@pytest.mark.parametrize("rounding", ["separate", "fused", "kitchen"])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_int8_decode_split_k_epilogues(m, n, k, rounding, out_dtype):
+    """M <= 32 runs the split-K cluster kernel (automatic choice): partial
+    int32 sums from every CTA of a cluster, reduced in the leader, then the
+    same epilogue rounding as every other path."""
+    rng = np.random.default_rng(m * 31 + n + k)
+    a = rng.integers(-127, 128, (m, k), dtype=np.int8)
+    w = rng.integers(-127, 128, (n, k), dtype=np.int8)
+    sa = (rng.random(m) * 0.02 + 0.001).astype(np.float32)
+    sb = (rng.random(n) * 0.02 + 0.001).astype(np.float32)
+    bias = rng.standard_normal(n).astype(np.float32)
+    acc = oracle.gemm_s8(a, w)
+    assert np.array_equal(rdna2_ops.int8_matmul(cuda(a), cuda(w).T).cpu().numpy(), acc)
+    ref = oracle.epilogue_s32(acc, sa, sb, bias, oracle.F32, EPI[rounding], ODT[out_dtype])
+    if rounding == "kitchen":
+        out = torch.empty((m, n), device="cuda", dtype=out_dtype)
+        qlinear.qgemm_raw(nat.KIND_I8, cuda(a), cuda(w), cuda(sa), cuda(sb), cuda(bias), nat.EPI_KITCHEN, out)
+    else:
+        out = rdna2_ops.int8_gemm_dequant(cuda(a), cuda(w).T, cuda(sa), cuda(sb), cuda(bias), rounding=rounding,
+                                          out_dtype=out_dtype)
+    assert same_bits(out, ref)
+
+
+@pytest.mark.parametrize("m", [3, 300])
+def test_back_to_back_launches_without_sync(m):
+    """The fused linear's GEMM is launched with programmatic serialization
+    and may start while its prologue runs.  Weights quantized by the
+    previous kernel, and a chain of linears each reading the previous one's
+    output, must give the same bits as the same calls synchronised one by
+    one."""
+    rng = np.random.default_rng(m)
+    k, n = 1024, 2048
+    w1 = torch.from_numpy((rng.standard_normal((n, k)) * 0.03).astype(np.float32)).cuda()
+    w2 = torch.from_numpy((rng.standard_normal((k, n)) * 0.03).astype(np.float32)).cuda()
+    x = torch.from_numpy(outlier_activations(rng, m, k)).cuda().half()
+
+    def chain(sync):
+        wq1, sw1 = qlinear.quantize_weight(w1, rotation_block=128)
+        if sync:
+            torch.cuda.synchronize()
+        y1 = rdna2_ops.w8a8_linear(x, wq1, sw1, None, rotation_block=128, out_dtype=torch.float16)
+        if sync:
+            torch.cuda.synchronize()
+        wq2, sw2 = qlinear.quantize_weight(w2, rotation_block=128)
+        if sync:
+            torch.cuda.synchronize()
+        y2 = rdna2_ops.w8a8_linear(y1, wq2, sw2, None, rotation_block=128, out_dtype=torch.float16)
+        # a GEMM whose weight operand the kernel just before it writes
+        qx, sx = rdna2_ops.act_quant(x, rotation_block=128)
+        wq3, sw3 = qlinear.quantize_weight(w1, rotation_block=128)
+        if sync:
+            torch.cuda.synchronize()
+        y3 = rdna2_ops.int8_gemm_dequant(qx, wq3.T, sx, sw3, None)
+        torch.cuda.synchronize()
+        return y1.clone(), y2.clone(), y3.clone()
+
+    ref = chain(True)
+    for _ in range(3):
+        got = chain(False)
+        for g, r in zip(got, ref):
+            assert same_bits(g, bits(r))
 
 
 # ----------------------------------------------------- prologue (act_quant)
