@@ -22,6 +22,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _native as nat
+from .convrot_checkpoint import check_current, source_stamp
 from .qlinear import qgemm_raw
 
 _GROUPS = (32, 64, 128)
@@ -59,13 +60,15 @@ class W4A16Weight:
     `tiles` int32 [T, K/64, 128, 8] with T = ceil(N/128) -- unsigned nibbles,
     element j = k % 8 of a word at nibble (j >> 1) + 4*(j & 1); `groups`
     int32 [T, K/group, 128] -- low half the scale, high half the zero point
-    zu, both in `dtype`.  Rows past N are zero."""
+    zu, both in `dtype`.  Rows past N are zero.  `source` stamps the
+    PackedInt4 it was prepared from (convrot_checkpoint.source_stamp)."""
     tiles: torch.Tensor
     groups: torch.Tensor
     n: int
     k: int
     group_size: int
     dtype: torch.dtype
+    source: tuple | None = None
 
     @property
     def bytes(self):
@@ -73,23 +76,33 @@ class W4A16Weight:
 
     def clone(self):
         return W4A16Weight(self.tiles.clone(), self.groups.clone(), self.n, self.k, self.group_size,
-                           self.dtype)
+                           self.dtype, self.source)
+
+    def is_current(self, p):
+        """False once PackedInt4 `p` changed since this pack was prepared."""
+        return self.source is None or self.source == source_stamp(p)
 
 
 @dataclass
 class W4A8Weight:
     """B200 W4A8 format (include/b2_qlinear.h, b2_w4a8_prepare): `tiles`
     uint8 bytes of u64 [T, K/128, 8, 128] unsigned nibbles in the int8-unpack
-    order; `groups` u64 [T, K/group, 128] = {fp32 scale, zu}."""
+    order; `groups` u64 [T, K/group, 128] = {fp32 scale, zu}.  `source`
+    stamps the PackedInt4 it was prepared from."""
     tiles: torch.Tensor
     groups: torch.Tensor
     n: int
     k: int
     group_size: int
+    source: tuple | None = None
 
     @property
     def bytes(self):
         return sum(t.numel() * t.element_size() for t in (self.tiles, self.groups))
+
+    def is_current(self, p):
+        """False once PackedInt4 `p` changed since this pack was prepared."""
+        return self.source is None or self.source == source_stamp(p)
 
 
 # ------------------------------------------------------------ CPU packer
@@ -217,7 +230,7 @@ def prepare_w4a16(p, dtype=torch.bfloat16):
         p.data.data_ptr(), int(p.layout == "kn"), int(p.order == "high"), p.scales.data_ptr(),
         p.zeros.data_ptr(), p.n, p.k, p.group_size, nat.DTYPE_CODE[dtype], tiles.data_ptr(),
         groups.data_ptr(), nat.stream_ptr(p.data.device)), "b2_w4a16_prepare")
-    return W4A16Weight(tiles, groups, p.n, p.k, p.group_size, dtype)
+    return W4A16Weight(tiles, groups, p.n, p.k, p.group_size, dtype, source_stamp(p))
 
 
 def quantize_w4a16(w, *, group_size=128, dtype=torch.bfloat16):
@@ -263,6 +276,8 @@ def int4_linear_a16(a, p, *, bias=None, method="dequant", prepared=None, tile=(6
     if method == "prepared":
         if not isinstance(prepared, W4A16Weight):
             raise ValueError("W4A16Weight prepared weight required")
+        if isinstance(p, PackedInt4):
+            check_current(prepared, p)
         wt = prepared
     else:
         _validate(p)
@@ -320,7 +335,7 @@ def prepare_w4a8(p):
         p.data.data_ptr(), int(p.layout == "kn"), int(p.order == "high"), p.scales.data_ptr(),
         p.zeros.data_ptr(), p.n, p.k, p.group_size, tiles.data_ptr(), groups.data_ptr(),
         nat.stream_ptr(p.data.device)), "b2_w4a8_prepare")
-    return W4A8Weight(tiles, groups, p.n, p.k, p.group_size)
+    return W4A8Weight(tiles, groups, p.n, p.k, p.group_size, source_stamp(p))
 
 
 def int4_linear_a8(a, p, a_scale, *, bias=None, method="dot4", tile=(64, 64), num_warps=4,
@@ -337,6 +352,8 @@ def int4_linear_a8(a, p, a_scale, *, bias=None, method="dot4", tile=(64, 64), nu
     reference and not needed.  integer=True returns the exact INT32 sum.
     """
     if isinstance(prepared, W4A8Weight):
+        if isinstance(p, PackedInt4):
+            check_current(prepared, p)
         wt = prepared
     else:
         _validate(p)
