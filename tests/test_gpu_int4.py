@@ -133,7 +133,7 @@ def test_w4a16_small_shapes(dtype, m, n, k, g):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("m", [1, 5, 16, 17, 40, 64, 100, 128, 129, 300])
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 16, 17, 40, 64, 100, 128, 129, 300])
 @pytest.mark.parametrize("g", [32, 128])
 def test_w4a16_schedules(dtype, m, g):
     """Stream-K (M <= 128: a CTA's range crosses tiles, group stages start
