@@ -58,7 +58,8 @@ int b2_pair_capacity(void);
  * (automatic there), 128-row swap-AB weight tiles split along K over the
  * CTAs of a thread-block cluster and reduced in the leader's shared memory.
  * A tuning and verification knob; INT8 results are identical for every
- * choice, floating kinds differ only in fp32 summation order.
+ * choice, floating kinds differ only in fp32 summation order; 9 = pair N=192
+ * with the TMA-store epilogue (6 for unaligned outputs).
  * No reference counterpart (the reference exposes tile keywords instead,
  * rdna2_ops/int8_gemm.py:195-214). */
 int b2_set_gemm_path(int path);

@@ -85,7 +85,7 @@ int b2_sm_count(void) { return b2::device_sm_count(); }
 int b2_pair_capacity(void) { return b2::pair_capacity(); }
 
 int b2_set_gemm_path(int path) {
-  if (path < 0 || path > 8) return fail();
+  if (path < 0 || path > 9) return fail();
   b2::set_gemm_path(path);
   return 0;
 }

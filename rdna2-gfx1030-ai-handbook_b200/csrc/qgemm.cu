@@ -1260,7 +1260,8 @@ static int choose_config(int64_t M, int64_t N) {
 // Kernel selection: 0 auto; 1 single-CTA (auto N tile); 2 pair (auto N tile);
 // 3 single BN=256; 4 single BN=128; 5 pair BN=256; 6 pair BN=192;
 // 7 pair BN=256 with the TMA-store epilogue (needs 16-byte aligned output rows);
-// 8 split-K swap-AB cluster kernel (M <= 32 only).
+// 8 split-K swap-AB cluster kernel (M <= 32 only); 9 pair BN=192 with the
+// TMA-store epilogue.
 static int g_force_path = 0;
 
 template <int KIND>
@@ -1275,6 +1276,7 @@ static cudaError_t dispatch(int cfg, const void* a, int64_t lda, const void* b, 
     case 6: return launch_pair<KIND, 192, 7, false>(a, lda, b, ldb, p, max_ctas, stream);
     // 6 stages + 32 KiB of output staging
     case 7: return launch_pair<KIND, 256, 6, true>(a, lda, b, ldb, p, max_ctas, stream);
+    case 9: return launch_pair<KIND, 192, 6, true>(a, lda, b, ldb, p, max_ctas, stream);
     case 8:
       return p.M <= 16 ? launch_splitk<KIND, 16, 8>(a, lda, b, ldb, p, stream)
                        : launch_splitk<KIND, 32, 5>(a, lda, b, ldb, p, stream);
@@ -1299,11 +1301,25 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
     // Staged TMA stores: whole 128-byte lines instead of 32 half-sector
     // stores per warp instruction; on the config-2 GEMM 107.5 us against
     // 129.0 us for the 7-stage st.global epilogue on the same box.
-    if (cfg == 5 && p.vec_ok) cfg = 7;
+    if (cfg == 5 && p.vec_ok) {
+      cfg = 7;
+      // 256x192 pair tiles when the waves of the two tile widths favour
+      // them: modelled time = waves x tile width, 192 weighted by 1.06 for
+      // its larger operand stream per MAC.  Graph-replayed A/B on one B200:
+      // 1024x3072x3072 15.4 -> 12.7 us, 2048x5120x5120 53.2 -> 42.7 us,
+      // 8192x3072x3072 67.2 -> 61.3 us; the config-2 GEMM stays on 256
+      // (102.4 against 104.5 us).
+      const int pairs = pair_capacity();
+      const int64_t tm2 = (p.M + 255) / 256;
+      const int64_t w256 = (tm2 * ((p.N + 255) / 256) + pairs - 1) / pairs;
+      const int64_t w192 = (tm2 * ((p.N + 191) / 192) + pairs - 1) / pairs;
+      if (pairs > 0 && static_cast<double>(w192) * 192.0 * 1.06 < static_cast<double>(w256) * 256.0) cfg = 9;
+    }
   }
   if (cfg == 2) cfg = 5;
   if (cfg == 1) cfg = wide ? 3 : 4;
   if (cfg == 7 && !p.vec_ok) cfg = 5;  // TMA stores need 16-byte aligned output rows
+  if (cfg == 9 && !p.vec_ok) cfg = 6;
   cudaError_t e = kind == kKindI8     ? dispatch<kKindI8>(cfg, a, lda, b, ldb, p, max_ctas, stream)
                   : kind == kKindE4M3 ? dispatch<kKindE4M3>(cfg, a, lda, b, ldb, p, max_ctas, stream)
                   : kind == kKindF16  ? dispatch<kKindF16>(cfg, a, lda, b, ldb, p, max_ctas, stream)

@@ -37,11 +37,12 @@ def set_gemm_path(path):
     with the output staged in shared memory and written by TMA stores; falls
     back to "pair256" for outputs whose rows are not 16-byte aligned),
     "splitk" (M <= 32: swap-AB tiles split along K over a thread-block
-    cluster; larger M take "auto").  INT8 results are bit-identical for every
+    cluster; larger M take "auto"), "pair192s" (256x192 pair tiles with
+    TMA stores; "pair192" for unaligned outputs).  INT8 results are bit-identical for every
     choice (floating kinds differ only in fp32 summation order); this is a
     tuning and verification knob."""
     code = {"auto": 0, "single": 1, "pair": 2, "single256": 3, "single128": 4, "pair256": 5,
-            "pair192": 6, "pair256s": 7, "splitk": 8}[path]
+            "pair192": 6, "pair256s": 7, "splitk": 8, "pair192s": 9}[path]
     nat.check(nat.library().b2_set_gemm_path(code), "b2_set_gemm_path")
 
 

@@ -47,7 +47,7 @@ def x_bits(xt):
     return bits(xt)
 
 
-@pytest.fixture(params=["single256", "single128", "pair256", "pair192", "pair256s", "splitk"])
+@pytest.fixture(params=["single256", "single128", "pair256", "pair192", "pair256s", "pair192s", "splitk"])
 def gemm_path(request):
     qlinear.set_gemm_path(request.param)
     yield request.param
