@@ -389,7 +389,11 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * rows_per_cta; base < M; base += row_step, ++it) {
     const int64_t row = base + r_local;
     const bool live = active && row < M;
-    float v[E];
+    // The slice lives in element pairs: every butterfly stage from h = 2
+    // up, the 1/sqrt(B) scaling and the quantizer run on Blackwell's packed
+    // fp32 instructions (two lanes per instruction, each lane rounded exactly
+    // like the scalar operation it replaces).
+    float2 w[E / 2];
     if constexpr (kPrefetch) {
 #pragma unroll
       for (int j = 0; j < E / 8; ++j) {
@@ -398,23 +402,35 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
         float f[8];
         unpack_raw<DT>(r8, f);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[8 * j + i] = f[i];
+        for (int i = 0; i < 4; ++i) w[4 * j + i] = make_float2(f[2 * i], f[2 * i + 1]);
       }
       if (base + row_step < M) issue(base + row_step);
     } else {
+      float v[E];
       load_slice<DT, E>(x, live ? row * ldx + static_cast<int64_t>(part) * E : 0, live, v);
+#pragma unroll
+      for (int i = 0; i < E / 2; ++i) w[i] = make_float2(v[2 * i], v[2 * i + 1]);
     }
 
     if (block > 1) {
+      // h = 1: the two elements of a pair
 #pragma unroll
-      for (int h = 1; h < E; h <<= 1) {
-        if (block > h) {
+      for (int i = 0; i < E / 2; ++i) {
+        const float a = w[i].x, b = w[i].y;
+        w[i] = make_float2(__fadd_rn(a, b), __fsub_rn(a, b));
+      }
+      // h = 2H for H = 1, 2, ...: pair i with pair i + H; a - b as
+      // fma(b, -1, a), one rounding of the exact difference.
+      const float2 neg1 = make_float2(-1.0f, -1.0f);
 #pragma unroll
-          for (int i = 0; i < E; ++i)
-            if (!(i & h)) {
-              const float a = v[i], b = v[i + h];
-              v[i] = __fadd_rn(a, b);
-              v[i + h] = __fsub_rn(a, b);
+      for (int H = 1; 2 * H < E; H <<= 1) {
+        if (block > 2 * H) {
+#pragma unroll
+          for (int i = 0; i < E / 2; ++i)
+            if (!(i & H)) {
+              const float2 a = w[i], b = w[i + H];
+              w[i] = __fadd2_rn(a, b);
+              w[i + H] = __ffma2_rn(b, neg1, a);
             }
         }
       }
@@ -422,20 +438,23 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
       // lanes of one block are consecutive and aligned); lower lane a + b,
       // upper lane a - b with a the lower lane's value.
       for (int d = 1; d * E < block; d <<= 1) {
-        const float sgn = (lane & d) ? -1.0f : 1.0f;
+        const float sg = (lane & d) ? -1.0f : 1.0f;
+        const float2 sg2 = make_float2(sg, sg);
 #pragma unroll
-        for (int i = 0; i < E; ++i) {
-          const float o = __shfl_xor_sync(0xffffffffu, v[i], d);
-          v[i] = __fmaf_rn(sgn, v[i], o);
+        for (int i = 0; i < E / 2; ++i) {
+          const float2 o = make_float2(__shfl_xor_sync(0xffffffffu, w[i].x, d),
+                                       __shfl_xor_sync(0xffffffffu, w[i].y, d));
+          w[i] = __ffma2_rn(w[i], sg2, o);
         }
       }
+      const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
-      for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], inv);
+      for (int i = 0; i < E / 2; ++i) w[i] = __fmul2_rn(w[i], inv2);
     }
 
     float amax = 0.0f;
 #pragma unroll
-    for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    for (int i = 0; i < E / 2; ++i) amax = fmaxf(fmaxf(amax, fabsf(w[i].x)), fabsf(w[i].y));
     const int sb = it % 3;
     if (live) atomicMax(&s_max[sb][r_local], __float_as_uint(amax));
     for (int i = tid; i < rows_per_cta; i += blockDim.x) s_max[(it + 1) % 3][i] = 0u;  // next iteration's
@@ -455,40 +474,51 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
       float s2 = sc;
       if (sc < 8.673617379884035e-19f) {         // 2^-60
         s2 = __fmul_rn(sc, 1.8446744073709552e19f);  // x 2^64, exact
+        const float2 k2 = make_float2(1.8446744073709552e19f, 1.8446744073709552e19f);
 #pragma unroll
-        for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], 1.8446744073709552e19f);
+        for (int i = 0; i < E / 2; ++i) w[i] = __fmul2_rn(w[i], k2);
       } else if (sc > 1.152921504606847e18f) {   // 2^60
         s2 = __fmul_rn(sc, 5.421010862427522e-20f);  // x 2^-64, exact for s
+        const float2 k2 = make_float2(5.421010862427522e-20f, 5.421010862427522e-20f);
 #pragma unroll
-        for (int i = 0; i < E; ++i) v[i] = __fmul_rn(v[i], 5.421010862427522e-20f);
+        for (int i = 0; i < E / 2; ++i) w[i] = __fmul2_rn(w[i], k2);
       }
       const float r = __frcp_rn(s2);
+      const float2 r2 = make_float2(r, r), ns2 = make_float2(-s2, -s2);
+      const float2 magic = make_float2(12582912.0f, 12582912.0f);
+      // codes of the pair i (Markstein, as code_markstein): y = v*r,
+      // e = v - s*y exactly, RN(v/s) = y + e*r, + 1.5*2^23 -> low byte
+      auto codes = [&](int i, uint32_t& lo, uint32_t& hi) {
+        const float2 y = __fmul2_rn(w[i], r2);
+        const float2 e = __ffma2_rn(ns2, y, w[i]);
+        const float2 z = __ffma2_rn(e, r2, y);
+        const float2 m = __fadd2_rn(z, magic);
+        lo = __float_as_uint(m.x);
+        hi = __float_as_uint(m.y);
+      };
 #pragma unroll
       for (int j = 0; j < E / 16; ++j) {
-        uint32_t w[4];
+        uint32_t o[4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint32_t c0 = code_markstein(v[16 * j + 4 * t], s2, r);
-          const uint32_t c1 = code_markstein(v[16 * j + 4 * t + 1], s2, r);
-          const uint32_t c2 = code_markstein(v[16 * j + 4 * t + 2], s2, r);
-          const uint32_t c3 = code_markstein(v[16 * j + 4 * t + 3], s2, r);
-          w[t] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+        for (int t2 = 0; t2 < 4; ++t2) {
+          uint32_t c0, c1, c2, c3;
+          codes(8 * j + 2 * t2, c0, c1);
+          codes(8 * j + 2 * t2 + 1, c2, c3);
+          o[t2] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
         }
-        *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     } else {
 #pragma unroll
       for (int j = 0; j < E / 16; ++j) {
-        uint32_t w[4];
+        uint32_t o[4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint32_t c0 = slow_int8(v[16 * j + 4 * t], sc);
-          const uint32_t c1 = slow_int8(v[16 * j + 4 * t + 1], sc);
-          const uint32_t c2 = slow_int8(v[16 * j + 4 * t + 2], sc);
-          const uint32_t c3 = slow_int8(v[16 * j + 4 * t + 3], sc);
-          w[t] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+        for (int t2 = 0; t2 < 4; ++t2) {
+          const float2 p0 = w[8 * j + 2 * t2], p1 = w[8 * j + 2 * t2 + 1];
+          o[t2] = __byte_perm(__byte_perm(slow_int8(p0.x, sc), slow_int8(p0.y, sc), 0x0040),
+                              __byte_perm(slow_int8(p1.x, sc), slow_int8(p1.y, sc), 0x0040), 0x5410);
         }
-        *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
     if (part == 0) scale[row] = sc;
