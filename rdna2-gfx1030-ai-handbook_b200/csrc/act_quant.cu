@@ -392,7 +392,9 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
     // The slice lives in element pairs: every butterfly stage from h = 2
     // up, the 1/sqrt(B) scaling and the quantizer run on Blackwell's packed
     // fp32 instructions (two lanes per instruction, each lane rounded exactly
-    // like the scalar operation it replaces).
+    // like the scalar operation it replaces).  No packed multiply feeds a
+    // packed add here: such a pair was measured to come out fused (one
+    // rounding) elsewhere, which the exact codes could not tolerate.
     float2 w[E / 2];
     if constexpr (kPrefetch) {
 #pragma unroll
