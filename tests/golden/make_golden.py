@@ -1,10 +1,11 @@
 #!/usr/bin/env python3
 """Generate golden vectors from the reference's own CPU-runnable code.
 
-Run in a container that has the reference checkout (default
-/root/reference); the GPU hosts only read the committed .npz output.
+Run on a machine that has the reference checkout (its path in
+--reference, or in the environment variable RDNA2_REFERENCE); the GPU hosts
+only read the committed .npz output.
 
-  python tests/golden/make_golden.py [--reference PATH]
+  python tests/golden/make_golden.py --reference PATH
 
 What runs from the reference (unmodified, imported from its source tree):
   * rdna2_ops.int4_weight_gemm_v07.pack_int4_cpu / unpack_int4_cpu
@@ -25,6 +26,7 @@ What runs from the reference (unmodified, imported from its source tree):
     of the exhaustive decode check in bench_dtype_gemm_v06.py:232-245.
 """
 import argparse
+import os
 import sys
 import types
 from pathlib import Path
@@ -196,8 +198,11 @@ def fp8_decode(out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, default=os.environ.get("RDNA2_REFERENCE"))
     cfg = ap.parse_args()
+    if cfg.reference is None:
+        ap.error("give the reference checkout with --reference or RDNA2_REFERENCE")
+    cfg.reference = Path(cfg.reference)
     sys.dont_write_bytecode = True
     torch.set_num_threads(2)
     print("int8 known-answer cases:", int8_known_answer(OUT))
