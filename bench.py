@@ -77,6 +77,16 @@ def synth_inputs(rng, m, k):
 
 
 # ------------------------------------------------------------- CPU oracle
+def host_threads():
+    """Host cores this process may run on.  torchrun sets OMP_NUM_THREADS=1
+    for every rank; the CPU legs run on rank 0 alone and pass this count to
+    the oracle explicitly, so they use every core either way."""
+    try:
+        return max(1, len(os.sched_getaffinity(0)))
+    except AttributeError:
+        return max(1, os.cpu_count() or 1)
+
+
 def cpu_run(rows, threads=0):
     """Time the oracle's full W8A8 linear on `rows` tokens of the workload."""
     import oracle
@@ -92,8 +102,7 @@ def cpu_run(rows, threads=0):
 
 
 def cpu_baseline(budget_s):
-    import oracle
-    threads = oracle.max_threads()
+    threads = host_threads()
     t1 = cpu_run(64, threads)
     rows = int(min(M, max(64, budget_s / max(t1 / 64, 1e-9))))
     rows = max(64, rows // 64 * 64)
@@ -108,8 +117,7 @@ def run_reference(args, rank):
     """--impl reference: the CPU oracle port on the host cores (rank 0 only)."""
     if rank != 0:
         return
-    import oracle
-    threads = oracle.max_threads()
+    threads = host_threads()
     t1 = cpu_run(64, threads)
     per_row = t1 / 64
     budget = 120.0 / max(1, args.steps + args.warmup)
@@ -413,7 +421,7 @@ def run_b200(args, rank, world, local_rank):
     if rank != 0:
         return
     cpu = None
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:  # the host baseline is an N=1 figure
         cpu = cpu_baseline(args.cpu_budget_s)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
