@@ -20,6 +20,11 @@ struct GemmParams {
   int epilogue;
   int vec_ok;          // output rows 16-byte aligned: vector stores allowed
   int* status;         // device status word for bounded waits
+  // Split-K kernel only: stream the first ring of weights before
+  // griddepcontrol.wait.  Set only by the fused linear, whose preceding
+  // kernel (its own activation prologue) never writes the weights; any other
+  // caller's previous kernel may, and its writes are visible only after the wait.
+  int weight_prefetch;
 };
 
 // Device address of the bounded-wait status word on the current device.

@@ -157,6 +157,7 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
   if (e != cudaSuccess) return static_cast<int>(e);
   b2::GemmParams p = make_params(M, N, K, sa, w_scale, w_scale_count, bias, bias_dtype, epilogue,
                                  out, out_dtype, ldc);
+  p.weight_prefetch = 1;  // the prologue just launched writes only q and sa
   return static_cast<int>(b2::run_qgemm(kind, q, ldq, w, ldw, p, 0, s));
 }
 

@@ -842,9 +842,11 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // The weights do not depend on the previous kernel (the activation
-    // prologue): the first ring's worth streams in before the wait.
+    // Inside the fused linear the weights do not depend on the previous
+    // kernel (its activation prologue): the first ring's worth streams in
+    // before the wait.  Other callers wait first (p.weight_prefetch == 0).
     const int pre = kb1 - kb0 < STAGES ? kb1 - kb0 : STAGES;
+    if (!p.weight_prefetch) griddep_wait();
     if (elect_one()) {
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], L::kStageBytes);
@@ -852,7 +854,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     __syncwarp();
-    griddep_wait();
+    if (p.weight_prefetch) griddep_wait();
     if (elect_one()) {
       for (int i = 0; i < pre; ++i)
         tma_load_2d(&tma_x, &full[i], smem + L::kOffX + i * L::kXBytes, (kb0 + i) * kKbElems, 0);

@@ -1,223 +1,202 @@
 """INT8 GEMM with an optional fused FP32 dequantization epilogue, on sm_100a.
 
-Drop-in for the reference module rdna2_ops/int8_gemm.py (same public names
-and signatures).  The contraction runs on tcgen05 kind::i8 tensor cores with
-TMEM accumulators (csrc/qgemm.cu) instead of the gfx1030 dot4 Triton kernels
-_int8_dot_dequant / _int8_dot_dequant_wrapped (int8_gemm.py:19-123).
+Public surface of the reference module rdna2_ops/int8_gemm.py (names,
+signatures and exception classes): int8_matmul (:195-200), int8_gemm_dequant
+(:203-214), moss_int8_gemm_candidate (:217-271), qwen_int8_gemm_candidate
+(:274-330).  The contraction runs on tcgen05 kind::i8 tensor cores with
+TMEM accumulators (csrc/qgemm.cu, C ABI b2_qgemm) instead of the gfx1030 dot4
+Triton kernels _int8_dot_dequant / _int8_dot_dequant_wrapped (:19-123).
 
-Kept from the reference contract:
-  * the scale order float(acc) * (row_scale * col_scale) (int8_gemm.py:53-63);
-  * rounding="separate" forbids multiply/add contraction, rounding="fused"
-    uses one FMA (int8_gemm.py:191);
-  * B is read through its strides, so weight.T needs no copy
-    (int8_gemm.py:39-40); other layouts are repacked once per call;
-  * validation and eager-only policy (int8_gemm.py:131-149);
-  * a fresh output per call (int8_gemm.py:178).
-Tile / warp / stage / group_m keywords are validated like the reference and
-otherwise ignored: the B200 kernel sizes its own persistent tiles.
-Extension: `out_dtype` (fp32 default) lets the epilogue cast straight to
-fp16/bf16.
+Numerical contract kept from the reference:
+  * epilogue value float(acc) * (row_scale * col_scale) (+ bias) in fp32
+    (:53-63); rounding="separate" rounds the product and the sum separately,
+    rounding="fused" uses one FMA (:191);
+  * B is read through its strides, so the weight.T view needs no copy
+    (:39-40); layouts the TMA cannot address are repacked per call;
+  * a fresh output per call (:178).
+The Triton launch keywords (tile, num_warps, num_stages, group_m, wrapped,
+partial_dot) are checked for the reference's domains and otherwise unused.
+Extension: `out_dtype` (fp32 default) casts in the epilogue to fp16/bf16.
 """
-from contextlib import contextmanager
+from __future__ import annotations
+
 import sys
+from contextlib import contextmanager
 
 import torch
 
+from . import _args
 from . import _native as nat
-from .qlinear import act_quant, qgemm_raw
+from ._args import require
+from ._patch import CandidateStats, scoped_patch
+from .qlinear import qgemm_raw, w8a8_linear
 
-_K_MAX = 131071
-
-
-def _validate(a, b, tile, num_warps, num_stages, group_m):
-    if a.ndim != 2 or b.ndim != 2 or a.shape[1] != b.shape[0]:
-        raise ValueError("Expected [M,K] @ [K,N]")
-    if a.dtype != torch.int8 or b.dtype != torch.int8:
-        raise TypeError("Both GEMM operands must be INT8")
-    if a.device.type != "cuda" or b.device != a.device:
-        raise ValueError("Inputs must share a CUDA device")
-    nat.require_device(a, b)
-    if any(s < 0 for s in a.stride() + b.stride()):
-        raise ValueError("Negative strides are unsupported")
-    if a.shape[1] > _K_MAX:
-        raise ValueError("K could overflow signed INT32 for arbitrary signed INT8 inputs")
-    if len(tile) != 3 or any(v < 16 or v > 256 or v & (v - 1) for v in tile):
-        raise ValueError("Tile dimensions must be powers of two in [16,256]")
-    if num_warps not in (4, 8) or num_stages not in (1, 2, 3) or group_m not in (1, 2, 4, 8):
-        raise ValueError("Unsupported launch configuration")
-    if torch.compiler.is_compiling() or torch.cuda.is_current_stream_capturing():
-        raise RuntimeError("Only explicit eager calls are supported")
+_ROUNDING = {"separate": nat.EPI_SEPARATE, "fused": nat.EPI_FMA}
+_KERNEL_INFO = {"name": "qgemm (tcgen05 kind::i8)", "arch": "sm_100a"}
 
 
-def _launch(a, b, a_scale, b_scale, bias, *, tile, num_warps, num_stages, group_m, rounding,
-            return_kernel, wrapped=False, partial_dot=False, out_dtype=torch.float32):
-    _validate(a, b, tile, num_warps, num_stages, group_m)
-    if partial_dot and not wrapped:
-        raise ValueError("partial_dot requires the explicitly wrapped-load variant")
-    dequant = a_scale is not None
-    m, k = a.shape
-    n = b.shape[1]
-    if rounding not in ("separate", "fused"):
-        raise ValueError("rounding must be separate or fused")
-    if dequant:
-        for value, size, label in ((a_scale, m, "a_scale"), (b_scale, n, "b_scale")):
-            if not isinstance(value, torch.Tensor):
-                raise TypeError(label + " must be a device tensor")
-            if value.device != a.device or value.dtype != torch.float32 or not value.is_contiguous():
-                raise ValueError(label + " must be contiguous FP32 on the input device")
-            if value.numel() != size and not (label == "b_scale" and value.numel() == 1):
-                raise ValueError(label + " has the wrong number of elements")
-            if torch.is_grad_enabled() and value.requires_grad:
-                raise ValueError("Autograd is unsupported")
-        if bias is not None:
-            if (bias.device != a.device or bias.numel() != n or not bias.is_contiguous()
-                    or bias.dtype not in (torch.float32, torch.float16, torch.bfloat16)):
-                raise ValueError("Bias must be a contiguous floating point vector of length N")
-            if torch.is_grad_enabled() and bias.requires_grad:
-                raise ValueError("Autograd is unsupported")
-        if out_dtype not in (torch.float32, torch.float16, torch.bfloat16):
-            raise TypeError("out_dtype must be fp32, fp16 or bf16")
-    out = torch.empty((m, n), device=a.device, dtype=out_dtype if dequant else torch.int32)
-    if m == 0 or n == 0:
-        return (out, None) if return_kernel else out
-    epilogue = (nat.EPI_SEPARATE if rounding == "separate" else nat.EPI_FMA) if dequant else nat.EPI_NONE
-    qgemm_raw(nat.KIND_I8, a, b.T, a_scale if dequant else None, b_scale if dequant else None,
-              bias if dequant else None, epilogue, out)
-    kernel = {"name": "qgemm_kernel<kind::i8>", "arch": "sm_100a"} if return_kernel else None
-    return (out, kernel) if return_kernel else out
+def _run(a, b, scales, bias, *, rounding, out_dtype, tuning, wrapped, partial_dot, return_kernel):
+    """Shared body of the two GEMM entry points.  `scales` is None for the
+    raw INT32 product, else the (row, column) fp32 scale pair."""
+    m, n, _, dev = _args.int8_operands(a, b)
+    _args.tuning_keywords(*tuning)
+    _args.eager_call()
+    require(wrapped or not partial_dot, ValueError,
+            "partial_dot requires the explicitly wrapped-load variant")
+    require(rounding in _ROUNDING, ValueError, f"rounding must be 'separate' or 'fused', got {rounding!r}")
+    if scales is None:
+        out = torch.empty((m, n), device=dev, dtype=torch.int32)
+        epilogue, a_scale, b_scale, bias = nat.EPI_NONE, None, None, None
+    else:
+        a_scale, b_scale = scales
+        _args.fp32_vector(a_scale, m, "a_scale", dev)
+        _args.fp32_vector(b_scale, n, "b_scale", dev, scalar_ok=True)
+        _args.bias_vector(bias, n, dev)
+        _args.no_autograd(a_scale, b_scale, bias)
+        _args.output_dtype(out_dtype)
+        out = torch.empty((m, n), device=dev, dtype=out_dtype)
+        epilogue = _ROUNDING[rounding]
+    if m and n:
+        qgemm_raw(nat.KIND_I8, a, b.T, a_scale, b_scale, bias, epilogue, out)
+    if return_kernel:
+        return out, (dict(_KERNEL_INFO) if m and n else None)
+    return out
 
 
 def int8_matmul(a, b, *, tile=(32, 64, 64), num_warps=4, num_stages=1,
                 group_m=4, return_kernel=False, wrapped=False, partial_dot=False):
-    """Exact INT8 -> INT32 matmul; accepts both [K,N] layouts without copying
-    the weight.T view (reference int8_gemm.py:195-200)."""
-    return _launch(a, b, None, None, None, tile=tile, num_warps=num_warps,
-                   num_stages=num_stages, group_m=group_m, rounding="separate",
-                   return_kernel=return_kernel, wrapped=wrapped, partial_dot=partial_dot)
+    """Exact INT8 x INT8 -> INT32 product of a [M,K] and b [K,N] (any
+    non-negative strides; the weight.T view of an [N,K] weight is read in
+    place)."""
+    return _run(a, b, None, None, rounding="separate", out_dtype=torch.int32,
+                tuning=(tile, num_warps, num_stages, group_m), wrapped=wrapped,
+                partial_dot=partial_dot, return_kernel=return_kernel)
 
 
 def int8_gemm_dequant(a, b, a_scale, b_scale, bias=None, *, tile=(32, 64, 64),
                       num_warps=4, num_stages=1, group_m=4,
                       rounding="separate", return_kernel=False, wrapped=False, partial_dot=False,
                       out_dtype=torch.float32):
-    """INT32 GEMM and row/scalar or row/column FP32 dequantization in one kernel
-    (reference int8_gemm.py:203-214).  Inputs are already quantized; a fresh
-    output is allocated.  Finite scales/bias are a precondition."""
-    return _launch(a, b, a_scale, b_scale, bias, tile=tile, num_warps=num_warps,
-                   num_stages=num_stages, group_m=group_m, rounding=rounding,
-                   return_kernel=return_kernel, wrapped=wrapped, partial_dot=partial_dot,
-                   out_dtype=out_dtype)
+    """INT8 GEMM with the row x column (or row x scalar) fp32 dequantization
+    and optional bias applied in the GEMM's epilogue.  Operands are already
+    quantized; finite scales and bias are the caller's precondition."""
+    return _run(a, b, (a_scale, b_scale), bias, rounding=rounding, out_dtype=out_dtype,
+                tuning=(tile, num_warps, num_stages, group_m), wrapped=wrapped,
+                partial_dot=partial_dot, return_kernel=return_kernel)
+
+
+# ------------------------------------------------------------------ MOSS
+def _moss_fused_linear(x, weight, weight_scale, bias, out_dtype, rotation_block):
+    """Kitchen's int8_linear contract (ConvRot, per-token quantization, GEMM,
+    fp32 "separate" epilogue with an fp32 bias) as one b2_quant_linear call."""
+    k = x.shape[-1]
+    require(k == weight.shape[-1], ValueError,
+            f"Input and weight inner dimensions differ: {k} vs {weight.shape[-1]}")
+    weight = weight.to(device=x.device)
+    col_scale = weight_scale.to(device=x.device, dtype=torch.float32).reshape(-1).contiguous()
+    require(col_scale.numel() in (1, weight.shape[0]), ValueError,
+            "Weight scale must be scalar or per output channel")
+    require(rotation_block is None or k % rotation_block == 0, ValueError,
+            f"ConvRot group size {rotation_block} does not divide K={k}")
+    bias32 = None if bias is None else bias.to(device=x.device, dtype=torch.float32).reshape(-1).contiguous()
+    return w8a8_linear(x, weight, col_scale, bias32, rotation_block=rotation_block,
+                       out_dtype=out_dtype, epilogue="separate")
 
 
 @contextmanager
 def moss_int8_gemm_candidate(*, tile=(32, 64, 64), num_warps=4, num_stages=1, group_m=4,
                              wrapped=False, partial_dot=False):
-    """Scoped replacement of Kitchen's eager int8_linear export (reference
-    int8_gemm.py:217-271).  Kitchen's input activation and residual helpers
-    are preserved; ConvRot + row quantization run in the fused sm_100a
-    prologue and the GEMM + "separate" epilogue in the tcgen05 kernel.
-    Unlike the reference, fp16/bf16 calls are accelerated too (the epilogue
-    casts to out_dtype); only unsupported shapes fall back to the saved export.
-    """
+    """Within the block, Kitchen's eager `int8_linear` export runs the fused
+    sm_100a linear: ConvRot and row quantization in the prologue kernel, the
+    tcgen05 GEMM with the "separate" fp32 epilogue after it.  Kitchen's
+    input-activation and residual helpers still run around it.  Unlike the
+    reference (fp32 only), fp16/bf16 inputs and outputs are accelerated;
+    other dtypes call the saved export.  Yields hit / fallback statistics."""
+    _args.tuning_keywords(tile, num_warps, num_stages, group_m)
+    require(wrapped or not partial_dot, ValueError,
+            "partial_dot requires the explicitly wrapped-load variant")
     from comfy_kitchen.backends import eager as backend
-    from comfy_kitchen.backends.eager import quantization as q
-    original = backend.int8_linear
-    stats = {"hits": 0, "fallbacks": 0, "shapes": {}}
+    from comfy_kitchen.backends.eager import quantization as kitchen_q
+    saved_export = backend.int8_linear
+    stats = CandidateStats()
 
-    def candidate(x, weight, weight_scale, bias=None, out_dtype=torch.bfloat16,
-                  convrot=False, convrot_groupsize=256, input_act=None,
-                  input_act_weight=None, input_act_eps=0.0,
-                  residual=None, residual_scale=None):
-        if x.dtype not in (torch.float32, torch.float16, torch.bfloat16) or out_dtype not in (
-                torch.float32, torch.float16, torch.bfloat16):
-            stats["fallbacks"] += 1
-            return original(x, weight, weight_scale, bias=bias, out_dtype=out_dtype,
-                            convrot=convrot, convrot_groupsize=convrot_groupsize,
-                            input_act=input_act, input_act_weight=input_act_weight,
-                            input_act_eps=input_act_eps, residual=residual,
-                            residual_scale=residual_scale)
-        x = q._apply_input_act(x, input_act, input_act_weight, input_act_eps)
-        if x.shape[-1] != weight.shape[-1]:
-            raise ValueError("Input and weight inner dimensions differ")
-        weight = weight.to(device=x.device)
-        ws = weight_scale.to(device=x.device, dtype=torch.float32).reshape(-1)
-        if ws.numel() not in (1, weight.shape[0]):
-            raise ValueError("Weight scale must be scalar or per output channel")
-        if convrot and x.shape[-1] % convrot_groupsize:
-            raise ValueError("ConvRot group size does not divide K")
-        shape = x.shape
-        a, sa = act_quant(x.reshape(-1, shape[-1]),
-                          rotation_block=convrot_groupsize if convrot else None)
-        bias32 = None if bias is None else bias.to(device=x.device, dtype=torch.float32).reshape(-1)
-        y = int8_gemm_dequant(a, weight.T, sa, ws.contiguous(), bias32, tile=tile,
-                              num_warps=num_warps, num_stages=num_stages, group_m=group_m,
-                              rounding="separate", wrapped=wrapped, partial_dot=partial_dot,
-                              out_dtype=out_dtype)
-        stats["hits"] += 1
-        key = str((a.shape[0], weight.shape[0], a.shape[1]))
-        stats["shapes"][key] = stats["shapes"].get(key, 0) + 1
-        return q._apply_residual(y.reshape(*shape[:-1], weight.shape[0]), residual, residual_scale)
+    def int8_linear(x, weight, weight_scale, bias=None, out_dtype=torch.bfloat16, convrot=False,
+                    convrot_groupsize=256, input_act=None, input_act_weight=None, input_act_eps=0.0,
+                    residual=None, residual_scale=None):
+        if x.dtype not in _args.FLOAT_DTYPES or out_dtype not in _args.FLOAT_DTYPES:
+            stats.fallback()
+            return saved_export(x, weight, weight_scale, bias=bias, out_dtype=out_dtype, convrot=convrot,
+                                convrot_groupsize=convrot_groupsize, input_act=input_act,
+                                input_act_weight=input_act_weight, input_act_eps=input_act_eps,
+                                residual=residual, residual_scale=residual_scale)
+        x = kitchen_q._apply_input_act(x, input_act, input_act_weight, input_act_eps)
+        y = _moss_fused_linear(x, weight, weight_scale, bias, out_dtype,
+                               convrot_groupsize if convrot else None)
+        stats.hit(x.numel() // max(1, x.shape[-1]), weight.shape[0], x.shape[-1])
+        return kitchen_q._apply_residual(y, residual, residual_scale)
 
-    backend.int8_linear = candidate
-    try:
+    with scoped_patch(backend, {"int8_linear": int8_linear}, "MOSS eager export"):
         yield stats
-    finally:
-        if backend.int8_linear is not candidate:
-            raise RuntimeError("MOSS eager export changed during the research context")
-        backend.int8_linear = original
+
+
+# ------------------------------------------------------------------ Qwen
+_QWEN_BRIDGE_SUFFIX = "RDNA2-Qwen21-INT8/rocm_int8_kitchen_patch.py"
+# bridge callable -> whether its weight scale is one value per output row
+_QWEN_WRAPPERS = (("triton_int8_linear", False), ("triton_int8_linear_per_row", True))
+
+
+def _loaded_qwen_bridge():
+    hits = [mod for mod in list(sys.modules.values())
+            if mod is not None and str(getattr(mod, "__file__", "")).endswith(_QWEN_BRIDGE_SUFFIX)]
+    require(len(hits) == 1, RuntimeError, "Expected one already-loaded Qwen patientx bridge")
+    return hits[0]
+
+
+def qwen_column_scale(weight_scale, n, device, per_row):
+    """The bridge's weight scale as the GEMM's column-scale operand: n
+    per-row values for the per-row wrapper; one value (a tensor of any
+    shape holding one element, or a Python number) otherwise."""
+    if per_row:
+        return weight_scale.reshape(n).to(device=device, dtype=torch.float32).contiguous()
+    if isinstance(weight_scale, torch.Tensor):
+        return weight_scale.to(device=device, dtype=torch.float32, non_blocking=True).reshape(-1).contiguous()
+    return torch.full((1,), float(weight_scale), device=device, dtype=torch.float32)
+
+
+def _qwen_linear(bridge_fn, per_row, stats, gemm_keywords):
+    quantize_rows = bridge_fn.__globals__["triton_quantize_rowwise"]
+
+    def linear(x, weight, weight_scale, bias=None, compute_dtype=torch.float16):
+        if x.dtype != torch.float32 or compute_dtype != torch.float32:
+            stats.fallback()
+            return bridge_fn(x, weight, weight_scale, bias=bias, compute_dtype=compute_dtype)
+        rows = x.reshape(-1, x.shape[-1])
+        codes, row_scale = quantize_rows(rows.float() if per_row else rows)
+        col_scale = qwen_column_scale(weight_scale, weight.shape[0], x.device, per_row)
+        y = int8_gemm_dequant(codes, weight.T, row_scale.reshape(-1).contiguous(), col_scale, bias,
+                              rounding="fused", **gemm_keywords)
+        stats.hit(codes.shape[0], weight.shape[0], codes.shape[1])
+        return y.reshape(*x.shape[:-1], weight.shape[0])
+
+    return linear
 
 
 @contextmanager
 def qwen_int8_gemm_candidate(patch_module=None, *, tile=(32, 64, 64), num_warps=4, num_stages=1,
                              group_m=4, wrapped=False, partial_dot=False):
-    """Scoped replacement of the patientx bridge's two GEMM wrappers (reference
-    int8_gemm.py:274-330): the bridge's own row quantizer stays in use, the
-    GEMM + FMA ("fused") epilogue runs on the sm_100a kernel."""
-    if patch_module is None:
-        found = [m for m in tuple(sys.modules.values()) if m is not None
-                 and str(getattr(m, "__file__", "")).endswith(
-                     "RDNA2-Qwen21-INT8/rocm_int8_kitchen_patch.py")]
-        if len(found) != 1:
-            raise RuntimeError("Expected one already-loaded Qwen patientx bridge")
-        patch_module = found[0]
-    names = ("triton_int8_linear", "triton_int8_linear_per_row")
-    originals = {name: getattr(patch_module, name) for name in names}
-    stats = {"hits": 0, "fallbacks": 0, "shapes": {}}
-    replacements = {}
-
-    def make_wrapper(original, per_row):
-        quantize = original.__globals__["triton_quantize_rowwise"]
-
-        def candidate(x, weight, weight_scale, bias=None, compute_dtype=torch.float16):
-            if x.dtype != torch.float32 or compute_dtype != torch.float32:
-                stats["fallbacks"] += 1
-                return original(x, weight, weight_scale, bias=bias, compute_dtype=compute_dtype)
-            shape = x.shape
-            x2d = x.reshape(-1, shape[-1])
-            a, sa = quantize(x2d.float() if per_row else x2d)
-            if per_row:
-                ws = weight_scale.reshape(weight.shape[0]).contiguous()
-            elif isinstance(weight_scale, torch.Tensor):
-                ws = weight_scale.to(x.device, non_blocking=True).reshape(-1)
-            else:
-                ws = torch.tensor([weight_scale], device=x.device, dtype=torch.float32)
-            y = int8_gemm_dequant(a, weight.T, sa.reshape(-1).contiguous(), ws, bias, tile=tile,
-                                  num_warps=num_warps, num_stages=num_stages, group_m=group_m,
-                                  rounding="fused", wrapped=wrapped, partial_dot=partial_dot)
-            stats["hits"] += 1
-            key = str((a.shape[0], weight.shape[0], a.shape[1]))
-            stats["shapes"][key] = stats["shapes"].get(key, 0) + 1
-            return y.reshape(*shape[:-1], weight.shape[0])
-        return candidate
-
-    for name, original in originals.items():
-        replacements[name] = make_wrapper(original, name.endswith("per_row"))
-        setattr(patch_module, name, replacements[name])
-    try:
+    """Within the block, the patientx Qwen bridge's two INT8 GEMM wrappers run
+    the sm_100a GEMM with the FMA ("fused") epilogue; the bridge's own row
+    quantizer stays in use, and non-fp32 calls go to the saved wrappers.
+    The bridge module is found among the loaded modules by its source path
+    unless given.  Yields hit / fallback statistics."""
+    _args.tuning_keywords(tile, num_warps, num_stages, group_m)
+    require(wrapped or not partial_dot, ValueError,
+            "partial_dot requires the explicitly wrapped-load variant")
+    bridge = patch_module if patch_module is not None else _loaded_qwen_bridge()
+    gemm_keywords = dict(tile=tile, num_warps=num_warps, num_stages=num_stages, group_m=group_m,
+                         wrapped=wrapped, partial_dot=partial_dot)
+    stats = CandidateStats()
+    replacements = {name: _qwen_linear(getattr(bridge, name), per_row, stats, gemm_keywords)
+                    for name, per_row in _QWEN_WRAPPERS}
+    with scoped_patch(bridge, replacements, "Qwen patientx callable"):
         yield stats
-    finally:
-        for name in names:
-            if getattr(patch_module, name) is not replacements[name]:
-                raise RuntimeError("Qwen patientx callable changed during the research context")
-        for name, original in originals.items():
-            setattr(patch_module, name, original)

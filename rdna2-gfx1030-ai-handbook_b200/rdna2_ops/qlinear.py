@@ -24,10 +24,11 @@ from __future__ import annotations
 
 import torch
 
+from . import _args
 from . import _native as nat
 
 EPILOGUES = {"separate": nat.EPI_SEPARATE, "fused": nat.EPI_FMA, "kitchen": nat.EPI_KITCHEN}
-FLOAT_DTYPES = (torch.float32, torch.float16, torch.bfloat16)
+FLOAT_DTYPES = _args.FLOAT_DTYPES
 
 
 def set_gemm_path(path):
@@ -165,23 +166,6 @@ def qgemm_raw(kind, a, w, a_scale, w_scale, bias, epilogue, out):
     return out
 
 
-def _check_scale(t, size, label, dev, allow_scalar=False):
-    if not isinstance(t, torch.Tensor):
-        raise TypeError(label + " must be a device tensor")
-    if t.device != dev or t.dtype != torch.float32 or not t.is_contiguous():
-        raise ValueError(label + " must be contiguous FP32 on the input device")
-    if t.numel() != size and not (allow_scalar and t.numel() == 1):
-        raise ValueError(label + " has the wrong number of elements")
-
-
-def _check_bias(bias, n, dev):
-    if bias is None:
-        return
-    if (bias.device != dev or bias.numel() != n or not bias.is_contiguous()
-            or bias.dtype not in FLOAT_DTYPES):
-        raise ValueError("Bias must be a contiguous floating point vector of length N")
-
-
 def w8a8_linear(x, w_q, w_scale, bias=None, *, rotation_block=None, out_dtype=None,
                 epilogue="separate", kind="int8", workspace=None):
     """y[..., N] = epilogue(quantize(rotate(x)) @ w_q.T) in one C call.
@@ -201,8 +185,8 @@ def w8a8_linear(x, w_q, w_scale, bias=None, *, rotation_block=None, out_dtype=No
     n, k = w_q.shape
     if x.shape[-1] != k:
         raise ValueError(f"Input and weight inner dimensions must match, got {x.shape[-1]} and {k}")
-    _check_scale(w_scale, n, "w_scale", dev, allow_scalar=True)
-    _check_bias(bias, n, dev)
+    _args.fp32_vector(w_scale, n, "w_scale", dev, scalar_ok=True)
+    _args.bias_vector(bias, n, dev)
     out_dtype = out_dtype or x.dtype
     x2 = _rows_2d(x)
     m = x2.shape[0]

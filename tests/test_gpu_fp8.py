@@ -4,12 +4,14 @@
   (finite bits equal to torch's native cast, NaN and +-Inf classes equal);
 * int8 methods: reference row quantizer (_quant_rows) codes/scales bit-exact,
   INT32 GEMM exact, fp32 epilogue bit-exact, cast to fp16;
-* float methods: fp16 output within 1 fp16 ulp plus 2^-12 of sum |a*w|
-  (exact products, fp32 accumulation in tensor-core order)."""
+* float methods and scaled e4m3: every output within 1 ulp of the output
+  type plus the fp32 accumulation term 2^-20 * sum|a*w| (exact products,
+  fp32 accumulation in tensor-core order; conftest.assert_within_ulp)."""
 import numpy as np
 import pytest
 
 import oracle
+from conftest import assert_within_ulp
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -89,26 +91,37 @@ def test_float_methods(method):
     bias = (torch.randn(n, device="cuda") * 0.05).half()
     prep = w.half() if method == "prepared_fp16" else None
     y = f8.fp8_weight_gemm(a, w, bias=bias, method=method, prepared=prep)
-    af = oracle.decode(_bits16(a), oracle.F16)
-    wf = _decoded(w)
-    ref = oracle.gemm_f32_f64(af, wf) + oracle.decode(_bits16(bias), oracle.F16)[None, :]
-    absref = oracle.gemm_f32_f64(np.abs(af), np.abs(wf))
-    got = oracle.decode(_bits16(y), oracle.F16).astype(np.float64)
-    tol = np.maximum(np.abs(ref), 2.0 ** -14) * 2.0 ** -11 + 2.0 ** -12 * absref
-    assert np.all(np.abs(got - ref) <= tol)
+    af = oracle.decode(_bits16(a), oracle.F16).astype(np.float64)
+    wf = _decoded(w).astype(np.float64)
+    ref = af @ wf.T + oracle.decode(_bits16(bias), oracle.F16).astype(np.float64)[None, :]
+    absref = np.abs(af) @ np.abs(wf).T
+    got = oracle.decode(_bits16(y), oracle.F16)
+    assert_within_ulp(got, ref, absref, "fp16", method)
 
 
-def test_scaled_e4m3_method_config4():
-    """BASELINE config 4 through the reference-named entry point."""
-    m, n, k = 2048, 5120, 5120
-    a = torch.randn((m, k), device="cuda").to(torch.bfloat16)
-    wf = torch.randn((n, k), device="cuda") * 0.02
+@pytest.mark.parametrize("m", [1, 2048])
+def test_scaled_e4m3_method_config4(m):
+    """BASELINE config 4 through the reference-named entry point
+    fp8_weight_gemm(method="scaled_e4m3"): activation codes bit-exact with the
+    oracle's per-token e4m3 quantizer, and every output within 1 bf16 ulp
+    plus the fp32 accumulation term of the exact f64 value."""
+    n = k = 5120
+    gen = torch.Generator(device="cuda").manual_seed(20261108 + m)
+    a = torch.randn((m, k), generator=gen, device="cuda").to(torch.bfloat16)
+    wf = torch.randn((n, k), generator=gen, device="cuda") * 0.02
     wq, sw = f8.prepare_scaled_e4m3_weight(wf)
     y = f8.fp8_weight_gemm(a, wq, method="scaled_e4m3", w_scale=sw)
     assert y.dtype == torch.bfloat16 and y.shape == (m, n)
-    ref = (a.float() @ wf.T)
-    rel = (y.float() - ref).norm() / ref.norm()
-    assert rel < 0.06          # e4m3 quantization of both operands, not a parity check
+    aq, sa = oracle.quant_rows_e4m3(oracle.decode(_bits16(a), oracle.BF16))
+    rq, rs = oracle.quant_rows_e4m3(wf.cpu().numpy())
+    assert np.array_equal(wq.view(torch.uint8).cpu().numpy(), rq)
+    assert np.array_equal(sw.cpu().numpy().view(np.uint32), rs.view(np.uint32))
+    a64 = oracle.decode_e4m3(aq).astype(np.float64)
+    w64 = oracle.decode_e4m3(rq).astype(np.float64)
+    scale = sa.astype(np.float64)[:, None] * rs.astype(np.float64)[None, :]
+    ref = (a64 @ w64.T) * scale
+    absref = (np.abs(a64) @ np.abs(w64).T) * scale
+    assert_within_ulp(oracle.decode(_bits16(y), oracle.BF16), ref, absref, "bf16", f"scaled_e4m3 M={m}")
 
 
 def test_rejects_bad_calls():

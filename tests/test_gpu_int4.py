@@ -4,12 +4,14 @@ the fp64 CPU oracle at every BASELINE config-3 token count.
 
 W4A16 tolerance: the dequantized 16-bit weights are bit-exact by
 construction; the GEMM accumulates exact fp32 products in an order the
-tensor core chooses, so outputs must lie within 1 ulp of the 16-bit output
-type at |ref| plus 2^-12 of the sum of |a*w| products (fp32 accumulation)."""
+tensor core chooses, so every output must lie within 1 ulp of the 16-bit
+output type plus the fp32 accumulation term 2^-20 * sum|a*w|
+(conftest.assert_within_ulp), checked on every output of every shape."""
 import numpy as np
 import pytest
 
 import oracle
+from conftest import assert_within_ulp
 
 torch = pytest.importorskip("torch")
 pytestmark = pytest.mark.gpu
@@ -99,22 +101,20 @@ def _ref_w4a16(a_bits, a_code, p_cpu, dtype):
     s16 = p_cpu.scales.to(dtype).float().numpy()
     w = oracle.dequant_int4(p_cpu.data.numpy(), s16, p_cpu.zeros.float().numpy(), p_cpu.group_size,
                             out_dtype=ODT[dtype])
-    a = oracle.decode(a_bits, a_code)
-    return oracle.gemm_f32_f64(a, w), oracle.gemm_f32_f64(np.abs(a), np.abs(w))
+    a = oracle.decode(a_bits, a_code).astype(np.float64)
+    w = w.astype(np.float64)
+    return a @ w.T, np.abs(a) @ np.abs(w).T
 
 
 def _bits(t):
     return t.detach().cpu().view(torch.int16).numpy().view(np.uint16)
 
 
-def _check(y, ref, absref, dtype, bias=None):
+def _check(y, ref, absref, dtype, bias=None, what="w4a16"):
     got = oracle.decode(_bits(y), ODT[dtype]).astype(np.float64)
     if bias is not None:
         ref = ref + oracle.decode(_bits(bias), ODT[dtype]).astype(np.float64)[None, :]
-    ulp = np.maximum(np.abs(ref), 2.0 ** -14) * (2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11)
-    tol = ulp + 2.0 ** -12 * absref
-    bad = np.abs(got - ref) > tol
-    assert not bad.any(), f"{bad.sum()} of {bad.size} outside tolerance"
+    assert_within_ulp(got, ref, absref, "bf16" if dtype == torch.bfloat16 else "fp16", what)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
@@ -150,24 +150,32 @@ def test_w4a16_schedules(dtype, m, g):
     _check(y, ref, absref, dtype, bias)
 
 
-@pytest.mark.parametrize("m", [1, 16, 128, 2048])
-def test_w4a16_config3(m):
-    """bf16 A [M,4096], W [14336,4096] N(0,0.02) affine uint4
-    g128 with bf16 scales/zeros, bf16 out; oracle on a row/column sample."""
-    dtype = torch.bfloat16
+@pytest.fixture(scope="module")
+def config3_pack():
+    """BASELINE config 3 weight: W [14336,4096] ~ N(0,0.02), affine uint4 g128,
+    packed on the CPU by pack_int4_cpu (the packer the reference goldens pin);
+    the device packer must produce the same pack."""
     n, k = 14336, 4096
-    gen = torch.Generator(device="cuda").manual_seed(20261107)
-    w = torch.randn((n, k), generator=gen, device="cuda") * 0.02
-    wt = i4.quantize_w4a16(w, group_size=128, dtype=dtype)
-    a = torch.randn((m, k), generator=gen, device="cuda").to(dtype)
-    y = i4.w4a16_gemm(a, wt)
-    rng = np.random.default_rng(m)
-    rows = np.arange(m) if m <= 64 else np.sort(rng.choice(m, 64, replace=False))
-    cols = np.sort(rng.choice(n, 384, replace=False))
-    p = i4.pack_int4(w[torch.from_numpy(cols).cuda()], group_size=128, symmetric=False)
-    p_cpu = p.to("cpu")
-    ref, absref = _ref_w4a16(_bits(a[torch.from_numpy(rows).cuda()]), ODT[dtype], p_cpu, dtype)
-    _check(y[torch.from_numpy(rows).cuda()][:, torch.from_numpy(cols).cuda()], ref, absref, dtype)
+    gen = torch.Generator().manual_seed(20261107)
+    w = torch.randn((n, k), generator=gen) * 0.02
+    p_cpu = i4.pack_int4_cpu(w, group_size=128, symmetric=False)
+    p_dev = i4.pack_int4(w.cuda(), group_size=128, symmetric=False)
+    for f in ("data", "scales", "zeros", "sums"):
+        assert torch.equal(getattr(p_dev, f).cpu().view(torch.int32), getattr(p_cpu, f).view(torch.int32)), f
+    return p_cpu, i4.prepare_w4a16(p_cpu.to("cuda"), torch.bfloat16)
+
+
+@pytest.mark.parametrize("m", [1, 16, 128, 2048])
+def test_w4a16_config3(m, config3_pack):
+    """bf16 A [M,4096] ~ N(0,1) against the CPU-packed
+    weight, bf16 out; every one of the M x 14336 outputs checked."""
+    dtype = torch.bfloat16
+    p_cpu, wt = config3_pack
+    gen = torch.Generator().manual_seed(20261107 + m)
+    a = torch.randn((m, p_cpu.k), generator=gen).to(dtype)
+    y = i4.w4a16_gemm(a.cuda(), wt)
+    ref, absref = _ref_w4a16(_bits(a), ODT[dtype], p_cpu, dtype)
+    _check(y, ref, absref, dtype, what=f"config3 M={m}")
 
 
 def test_w4a16_deterministic_split_k():
