@@ -9,12 +9,14 @@ per-token INT8 quantization (prologue kernel) -> tcgen05 kind::i8 GEMM
 against the rotated, per-channel-quantized weight W[12288,3072] with the
 fused scale/bias/fp16 epilogue.  Metric: TOPS = 2*M*N*K / step time.
 
-Multi-GPU (torchrun, one rank per GPU, NCCL): column-parallel N-sharding with
-weak scaling -- every rank owns a [12288,3072] column shard of a
-[12288*P,3072] weight and computes its [4096,12288] output block from the
-replicated activations.  The NCCL all-gather that reassembles the full output
-is timed separately and reported under "allgather" (it is not needed by a
-consumer that reads the sharded output).
+Multi-GPU (torchrun, one rank per GPU): column-parallel N-sharding of the
+same config-2 layer (strong scaling: each of P ranks owns 12288/P output
+columns), with the output reassembled on every rank INSIDE the step: the
+GEMM epilogue writes each output tile into every rank's full Y over NVLink
+(b2_quant_linear_gather) and the step ends when every rank has all of Y
+(b2_gather_wait).  Side figures: the same step with an NCCL all-gather
+instead, the rank-local linear alone, and weak scaling (12288 columns per
+rank, gather included).
 
 The reference arm (--impl reference) times the CPU oracle -- the reference's
 math restated in C (oracle/) -- on the host cores over a bounded sample of
@@ -113,6 +115,67 @@ def cpu_baseline(budget_s):
                       f"on {rows} of {M} tokens x N={N} x K={K}, {dt:.2f} s, {threads} OpenMP threads"}
 
 
+def _hadamard(b):
+    """Orthonormal Sylvester Hadamard matrix of order b (fp32)."""
+    import torch
+    h = torch.ones((1, 1))
+    while h.shape[0] < b:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    return h / float(b) ** 0.5
+
+
+def torch_cpu_linear(x16, h, wq, sw, bias16):
+    """The reference's PyTorch math for the MOSS INT8 linear, on the CPU:
+    block rotation by a matmul with the orthonormal Hadamard
+    (production/MOSS_RDNA2_INT8/backend.py:112-118), per-row absmax/127
+    round-half-even INT8 (the quantize_int8_rowwise call, :122), the exact
+    INT8 GEMM (torch._int_mm in the role of the backend's
+    _int8_matmul_accumulate), and the epilogue
+    (acc.float() * (sx * sw)).to(out) + bias (:128-145)."""
+    import torch
+    m, k = x16.shape
+    b = h.shape[0]
+    xr = (x16.float().reshape(m, k // b, b) @ h).reshape(m, k)
+    amax = xr.abs().amax(1, keepdim=True)
+    sx = torch.where(amax > 0, amax / 127.0, torch.ones_like(amax))
+    q = torch.clamp(torch.round(xr / sx), -127, 127).to(torch.int8)
+    acc = torch._int_mm(q, wq.T)
+    return (acc.float() * (sx * sw[None, :])).to(torch.float16) + bias16
+
+
+def torch_cpu_baseline(budget_s, threads):
+    """The torch CPU leg on `threads` host threads over a bounded token
+    sample of the config-2 workload (the same op count per token)."""
+    import torch
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        g = torch.Generator().manual_seed(SEED)
+        w = torch.randn((N, K), generator=g) * 0.02
+        h = _hadamard(ROT)
+        wr = (w.reshape(N, K // ROT, ROT) @ h).reshape(N, K)
+        sw = wr.abs().amax(1) / 127.0
+        wq = torch.clamp(torch.round(wr / sw[:, None]), -127, 127).to(torch.int8)
+        bias = (torch.randn(N, generator=g) * 0.02).half()
+
+        def run(rows):
+            x = torch.from_numpy(synth_inputs(np.random.default_rng(SEED), rows, K)).half()
+            t0 = time.perf_counter()
+            torch_cpu_linear(x, h, wq, sw, bias)
+            return time.perf_counter() - t0
+
+        run(64)
+        t1 = run(64)
+        rows = int(min(M, max(64, 0.5 * budget_s / max(t1 / 64, 1e-9)))) // 64 * 64
+        dt = min(run(rows), run(rows))  # the first large call also pays page faults
+    finally:
+        torch.set_num_threads(prev)
+    return {"value": round(2.0 * rows * N * K / dt / 1e12, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"torch CPU restatement of the reference's linear math (matmul rotation, rowwise INT8, "
+                      f"torch._int_mm, backend.py epilogue) on {rows} of {M} tokens x N={N} x K={K}, {dt:.2f} s, "
+                      f"{threads} torch threads"}
+
+
 def run_reference(args, rank):
     """--impl reference: the CPU oracle port on the host cores (rank 0 only)."""
     if rank != 0:
@@ -206,6 +269,69 @@ class ClockSampler:
                 "samples": len(self.samples)}
 
 
+def e2e_pipeline(torch, dev, stream, xs, linear, out_shape, n_e, barrier):
+    """End-to-end steps through a public call with host buffers: every step
+    uploads its X from pinned host memory and reads its Y back into pinned
+    host memory.  Uploads run on one copy stream, the linear on the compute
+    stream and read-backs on another copy stream, double buffered, so step
+    i's read-back overlaps step i+1's upload and linear (PCIe is full duplex)
+    -- how a serving loop streams requests through the call.  Every step's
+    copies stay inside the timed region.  The last output read back is
+    checked against a direct call.  Returns ms per step on this rank."""
+    m, k = xs[0].shape
+    x_host = [xs[b].cpu().pin_memory() for b in range(2)]
+    y_host = [torch.empty(out_shape, dtype=torch.float16).pin_memory() for _ in range(2)]
+    xd = [torch.empty((m, k), device=dev, dtype=torch.float16) for _ in range(2)]
+    s_up, s_down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    up = [torch.cuda.Event() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    down = [torch.cuda.Event() for _ in range(2)]
+    started = [False, False]
+
+    def e2e_step(i):
+        b = i % 2
+        with torch.cuda.stream(s_up):
+            if started[b]:
+                s_up.wait_event(done[b])        # the linear of step i-2 has read xd[b]
+            xd[b].copy_(x_host[b], non_blocking=True)
+            up[b].record(s_up)
+        stream.wait_event(up[b])
+        if started[b]:
+            stream.wait_event(down[b])          # y_host[b] of step i-2 is home (the buffer is reused)
+        y = linear(xd[b])
+        done[b].record(stream)
+        with torch.cuda.stream(s_down):
+            s_down.wait_event(done[b])
+            y_host[b].copy_(y, non_blocking=True)
+            y.record_stream(s_down)
+            down[b].record(s_down)
+        started[b] = True
+
+    def drain():
+        for b in range(2):
+            if started[b]:
+                stream.wait_event(down[b])
+
+    for i in range(4):
+        e2e_step(i)
+    drain()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(n_e):
+        e2e_step(i)
+    drain()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n_e
+    ref_y = linear(xd[(n_e - 1) % 2]).cpu()
+    assert torch.equal(y_host[(n_e - 1) % 2].view(torch.int16), ref_y.view(torch.int16)), \
+        "pipelined end-to-end output differs from a direct call"
+    return ms
+
+
 # ------------------------------------------------------------------ B200
 def run_b200(args, rank, world, local_rank):
     import torch
@@ -218,9 +344,8 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     lib = nat.library()
     gen = torch.Generator(device=dev)
-    gen.manual_seed(SEED + rank)
+    gen.manual_seed(SEED)
 
-    # Weight shard for this rank (config 2 weight per rank: weak scaling).
     w = torch.randn((N, K), generator=gen, device=dev) * 0.02
     wq, sw = qlinear.quantize_weight(w, rotation_block=ROT)
     del w
@@ -248,8 +373,7 @@ def run_b200(args, rank, world, local_rank):
             nat.check(st, "b2_quant_linear")
 
     def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local_rank])
+        pass  # one rank
 
     for i in range(max(3, args.warmup)):
         step(i)
@@ -268,13 +392,19 @@ def run_b200(args, rank, world, local_rank):
         e1.record(stream)
         torch.cuda.synchronize()
         t_wall = time.perf_counter() - t_wall
-    barrier()
     ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = t.item()
-    value = world * 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    value = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+
+    # ---- sustained: the same step back to back for >= 1 s (clock record beside it)
+    n_sus = max(args.steps, int(1.0 / (ms * 1e-3)) + 1)
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as sus_clocks:
+        e0.record(stream)
+        for i in range(n_sus):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    sus_ms = e0.elapsed_time(e1) / n_sus
 
     # ---- dominant kernel alone (GEMM on pre-quantized activations), same stream
     qa, sa = rdna2_ops.act_quant(xs[0], rotation_block=ROT)
@@ -324,118 +454,36 @@ def run_b200(args, rank, world, local_rank):
     pk = peaks()
     int8_peak = 2.0 * pk["bf16_tflops"]
     achieved = 2.0 * M * N * K / (gemm_ms * 1e-3) / 1e12
-    traffic = None
-    prof = ROOT / "profiles" / "qgemm_pair_c2.md"
-    if prof.exists():
-        hit = re.search(r"dram_bytes_per_launch \| (\d+)", prof.read_text())
-        traffic = int(hit.group(1)) if hit else None
 
     # ---- end to end through the public API with host buffers
-    # Every step uploads its X from pinned host memory and reads its Y back
-    # into pinned host memory.  Uploads run on one copy stream, the linear on
-    # the compute stream and read-backs on another copy stream, double
-    # buffered, so step i's read-back overlaps step i+1's upload and linear
-    # (PCIe is full duplex) -- how a serving loop streams requests through
-    # the call.  Each step's copies stay inside the timed region.
-    x_host = [xs[b].cpu().pin_memory() for b in range(2)]
-    y_host = [torch.empty((M, N), dtype=torch.float16).pin_memory() for _ in range(2)]
-    xd = [torch.empty((M, K), device=dev, dtype=torch.float16) for _ in range(2)]
-    s_up, s_down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    up = [torch.cuda.Event() for _ in range(2)]
-    done = [torch.cuda.Event() for _ in range(2)]
-    down = [torch.cuda.Event() for _ in range(2)]
-    w_scale = sw
-    started = [False, False]
-
-    def e2e_step(i):
-        b = i % 2
-        with torch.cuda.stream(s_up):
-            if started[b]:
-                s_up.wait_event(done[b])        # the linear of step i-2 has read xd[b]
-            xd[b].copy_(x_host[b], non_blocking=True)
-            up[b].record(s_up)
-        stream.wait_event(up[b])
-        if started[b]:
-            stream.wait_event(down[b])          # y_host[b] of step i-2 is home (the buffer is reused)
-        y = rdna2_ops.w8a8_linear(xd[b], wq, w_scale, bias, rotation_block=ROT,
-                                  out_dtype=torch.float16, workspace=workspace)
-        done[b].record(stream)
-        with torch.cuda.stream(s_down):
-            s_down.wait_event(done[b])
-            y_host[b].copy_(y, non_blocking=True)
-            y.record_stream(s_down)
-            down[b].record(s_down)
-        started[b] = True
-
-    def drain():
-        for b in range(2):
-            if started[b]:
-                stream.wait_event(down[b])
-
-    for i in range(4):
-        e2e_step(i)
-    drain()
-    torch.cuda.synchronize()
-    n_e = max(10, min(100, args.steps // 5))
-    barrier()
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for i in range(n_e):
-        e2e_step(i)
-    drain()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / n_e
-    ref_y = rdna2_ops.w8a8_linear(xd[(n_e - 1) % 2], wq, w_scale, bias, rotation_block=ROT,
-                                  out_dtype=torch.float16, workspace=workspace).cpu()
-    assert torch.equal(y_host[(n_e - 1) % 2].view(torch.int16), ref_y.view(torch.int16)), \
-        "pipelined end-to-end output differs from a direct call"
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = t.item()
-
-    # ---- all-gather that reassembles the column-parallel output (reported apart)
-    gather = None
-    if world > 1:
-        full = torch.empty((world * M, N), device=dev, dtype=torch.float16)
-        for _ in range(3):
-            dist.all_gather_into_tensor(full, out)
-        torch.cuda.synchronize()
-        barrier()
-        e0.record(stream)
-        for _ in range(10):
-            dist.all_gather_into_tensor(full, out)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        g_ms = e0.elapsed_time(e1) / 10
-        t = torch.tensor([g_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        g_ms = t.item()
-        gather = {"ms": round(g_ms, 4), "bytes_per_rank_received": (world - 1) * M * N * 2,
-                  "busbw_gbs": round((world - 1) * M * N * 2 / (g_ms * 1e-3) / 1e9, 1),
-                  "value_including_gather": round(world * 2.0 * M * N * K / ((ms + g_ms) * 1e-3) / 1e12, 2)}
-        del full
+    e2e_ms = e2e_pipeline(torch, dev, stream, xs,
+                          lambda xd: rdna2_ops.w8a8_linear(xd, wq, sw, bias, rotation_block=ROT,
+                                                           out_dtype=torch.float16, workspace=workspace),
+                          (M, N), max(10, min(100, args.steps // 5)), barrier)
 
     status = nat.device_status()
     if rank != 0:
         return
-    cpu = None
-    if not args.no_cpu_baseline and world == 1:  # the host baseline is an N=1 figure
+    cpu = cpu_torch = cpu_torch2 = None
+    if not args.no_cpu_baseline:  # host baselines are N=1 figures
         cpu = cpu_baseline(args.cpu_budget_s)
+        cpu_torch = torch_cpu_baseline(args.cpu_budget_s, host_threads())
+        cpu_torch2 = torch_cpu_baseline(args.cpu_budget_s, 2)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic",
         "config": {"workload": "config2: W8A8 INT8 linear with block-128 Hadamard rotation, "
                                "fp16 X[4096,3072] (1% outlier channels x20) -> fp16 Y[4096,12288]",
-                   "M": M, "N_per_rank": N, "K": K, "rotation_block": ROT,
-                   "parallelism": f"column-parallel N-shard x{world}" if world > 1 else "single GPU",
+                   "M": M, "N": N, "N_per_rank": N, "K": K, "rotation_block": ROT,
+                   "parallelism": "single GPU",
                    "l2": f"inputs cycled over {args.sets} buffer sets "
                          f"({args.sets * (M * K * 2 + N * K) / 2**20:.0f} MiB > 126 MB L2)"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
-                     "unit": "TOPS", "frac": round(achieved / int8_peak, 4), "traffic": traffic,
+                     "unit": "TOPS", "frac": round(achieved / int8_peak, 4), "traffic": None,
+                     "traffic_note": "not measured in this run (no profiler inside the bench); the ncu capture "
+                                     "of this kernel on this workload is summarised in profiles/",
                      "kernel": "qgemm_pair_kernel<kind::i8,BN=256> (auto path on C2)",
                      "peak_source": f"2 x bf16_tflops ({pk['source']}): kind::i8 issues at twice "
                                     "the kind::f16 rate",
@@ -443,7 +491,11 @@ def run_b200(args, rank, world, local_rank):
                      "gemm_ms": round(gemm_ms, 5), "prologue_ms": round(pro_ms, 5),
                      "prologue_gbs": round((M * K * 2 + M * K + M * 4) / (pro_ms * 1e-3) / 1e9, 1)},
         "cpu_baseline": cpu,
-        "e2e": {"value": round(world * 2.0 * M * N * K / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT,
+        "cpu_baseline_torch": cpu_torch,
+        "cpu_baseline_torch_2threads": cpu_torch2,
+        "sustained": {"value": round(2.0 * M * N * K / (sus_ms * 1e-3) / 1e12, 2), "ms_per_step": round(sus_ms, 5),
+                      "steps": n_sus, "seconds": round(sus_ms * n_sus * 1e-3, 3), "clocks": sus_clocks.summary()},
+        "e2e": {"value": round(2.0 * M * N * K / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT,
                 "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": M * N * 2,
                 "api": "rdna2_ops.w8a8_linear (C ABI b2_quant_linear), pinned host X in, Y out, "
                        "uploads / linear / read-backs on three streams, double buffered",
@@ -453,8 +505,284 @@ def run_b200(args, rank, world, local_rank):
         "device_status": status,
         "wall_s_timed": round(t_wall, 4),
     }
-    if gather:
-        line["allgather"] = gather
+    print(json.dumps(line), flush=True)
+
+
+def _max_over_ranks(torch, dist, dev, value):
+    t = torch.tensor([value], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+def run_b200_multi(args, rank, world, local_rank):
+    """N > 1: config 2 column-parallel over the ranks with the output gather
+    inside every step (strong scaling; weak scaling and the NCCL gather as
+    side figures).  Every rank generates the same X and full weight from the
+    same seed and keeps its shard."""
+    import torch
+    import torch.distributed as dist
+    import rdna2_ops
+    from rdna2_ops import _native as nat
+    from rdna2_ops import qlinear
+    from rdna2_ops.column_parallel import PeerGather
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    lib = nat.library()
+    stream = torch.cuda.current_stream(dev)
+    sptr = stream.cuda_stream
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED)
+    w = torch.randn((N, K), generator=gen, device=dev) * 0.02
+    wq_full, sw_full = qlinear.quantize_weight(w, rotation_block=ROT)
+    del w
+    bias_full = (torch.randn(N, generator=gen, device=dev) * 0.02).half()
+    xs = []
+    for _ in range(args.sets):
+        x = torch.randn((M, K), generator=gen, device=dev)
+        idx = torch.randperm(K, generator=gen, device=dev)[: round(0.01 * K)]
+        x[:, idx] *= 20.0
+        xs.append(x.half())
+    ns = N // world
+    c0 = rank * ns
+    wq = wq_full[c0:c0 + ns].contiguous()
+    sw = sw_full[c0:c0 + ns].contiguous()
+    bias = bias_full[c0:c0 + ns].contiguous()
+    wqs = [wq] + [wq.clone() for _ in range(args.sets - 1)]
+    ws_bytes = lib.b2_quant_linear_workspace_bytes(M, K)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    g = PeerGather(M * N * world, torch.float16)   # also holds the weak-scaling output (N * world columns)
+
+    def gather_step(i, w_rows, sw_rows, b_rows, n_total, col0):
+        s = i % args.sets
+        epoch, slot = g.next_slot()
+        st = lib.b2_quant_linear_gather(nat.KIND_I8, xs[s].data_ptr(), nat.F16, M, K, K, ROT,
+                                        w_rows[s].data_ptr(), K, w_rows[s].shape[0], sw_rows.data_ptr(),
+                                        sw_rows.numel(), b_rows.data_ptr(), nat.F16, nat.EPI_SEPARATE, nat.F16,
+                                        n_total, col0, world, rank, g.outs[slot], g.states, epoch,
+                                        ws.data_ptr(), ws_bytes, sptr)
+        if st:
+            nat.check(st, "b2_quant_linear_gather")
+        g.wait(epoch, sptr)
+        return slot
+
+    def strong(i):
+        return gather_step(i, wqs, sw, bias, N, c0)
+
+    def barrier():
+        dist.barrier(device_ids=[local_rank])
+
+    def timed(fn, steps, sample_clocks=False):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sampler = ClockSampler(local_rank) if sample_clocks else None
+        if sampler:
+            sampler.__enter__()
+        t_wall = time.perf_counter()
+        e0.record(stream)
+        for i in range(steps):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter() - t_wall
+        if sampler:
+            sampler.__exit__()
+        barrier()
+        return _max_over_ranks(torch, dist, dev, e0.elapsed_time(e1) / steps), t_wall, sampler
+
+    # ---- correctness once: every rank holds the whole single-GPU result
+    slot = strong(0)
+    torch.cuda.synchronize()
+    ref = rdna2_ops.w8a8_linear(xs[0], wq_full, sw_full, bias_full, rotation_block=ROT, out_dtype=torch.float16)
+    got = g.local[slot][: M * N].view(M, N)
+    assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), "gathered output differs from 1-GPU linear"
+    del ref, wq_full
+    for i in range(max(3, args.warmup)):
+        strong(i)
+    torch.cuda.synchronize()
+    nat.device_status(reset=True)
+
+    # ---- timed region: K strong-scaling steps, gather inside
+    ms, t_wall, clocks = timed(strong, args.steps, sample_clocks=True)
+    value = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+
+    # ---- side figures (same discipline, fewer steps)
+    n_side = max(20, min(args.steps, 200))
+    out_local = torch.empty((M, ns), device=dev, dtype=torch.float16)
+
+    def local(i):
+        s = i % args.sets
+        nat.check(lib.b2_quant_linear(nat.KIND_I8, xs[s].data_ptr(), nat.F16, M, K, K, ROT, wqs[s].data_ptr(), K, ns,
+                                      sw.data_ptr(), ns, bias.data_ptr(), nat.F16, nat.EPI_SEPARATE,
+                                      out_local.data_ptr(), nat.F16, ns, ws.data_ptr(), ws_bytes, sptr),
+                  "b2_quant_linear")
+
+    for i in range(3):
+        local(i)
+    local_ms, _, _ = timed(local, n_side)
+    gathered = torch.empty((world * M, ns), device=dev, dtype=torch.float16)
+
+    def nccl(i):
+        local(i)
+        dist.all_gather_into_tensor(gathered, out_local)
+
+    for i in range(3):
+        nccl(i)
+    nccl_ms, _, _ = timed(nccl, n_side)
+    del gathered
+    # end to end: X uploaded to every rank, the rank's columns computed by the
+    # public call and read back over the rank's own PCIe link; the host holds
+    # Y by column shards (no device gather: the consumer is the host)
+    e2e_ms = e2e_pipeline(torch, dev, stream, xs,
+                          lambda xd: rdna2_ops.w8a8_linear(xd, wq, sw, bias, rotation_block=ROT,
+                                                           out_dtype=torch.float16, workspace=ws),
+                          (M, ns), max(10, min(100, args.steps // 5)), barrier)
+    e2e_ms = _max_over_ranks(torch, dist, dev, e2e_ms)
+    # weak scaling: a 12288-column shard per rank of a (12288 * P)-column layer
+    gen_w = torch.Generator(device=dev)
+    gen_w.manual_seed(SEED + 1 + rank)
+    w = torch.randn((N, K), generator=gen_w, device=dev) * 0.02
+    wq_w, sw_w = qlinear.quantize_weight(w, rotation_block=ROT)
+    del w
+    b_w = (torch.randn(N, generator=gen_w, device=dev) * 0.02).half()
+    wq_ws = [wq_w] + [wq_w.clone() for _ in range(args.sets - 1)]
+    del wqs
+
+    def weak(i):
+        return gather_step(i, wq_ws, sw_w, b_w, N * world, rank * N)
+
+    for i in range(3):
+        weak(i)
+    weak_ms, _, _ = timed(weak, n_side)
+    del wq_ws
+    status = nat.device_status()
+    g.close()
+    if rank != 0:
+        return
+    pk = peaks()
+    int8_peak = 2.0 * pk["bf16_tflops"]
+    nvlink_gbs = 770.0
+    recv = (world - 1) * M * ns * 2                   # bytes every rank must receive per step
+    t_gemm = 2.0 * M * ns * K / (int8_peak * 1e12) * 1e3
+    t_link = recv / (nvlink_gbs * 1e9) * 1e3
+    target = max(t_gemm, t_link)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic",
+        "config": {"workload": "config2 column-parallel: W8A8 INT8 linear with block-128 Hadamard rotation, "
+                               "fp16 X[4096,3072] -> fp16 Y[4096,12288], N sharded over the ranks, Y reassembled "
+                               "on every rank inside the step",
+                   "M": M, "N": N, "N_per_rank": ns, "K": K, "rotation_block": ROT,
+                   "parallelism": f"column-parallel N-shard x{world}, output gather fused into the GEMM epilogue "
+                                  "(NVLink peer stores)",
+                   "l2": f"inputs cycled over {args.sets} buffer sets, output buffers alternate (> 126 MB L2)"},
+        "roofline": {"bound": "nvlink" if t_link >= t_gemm else "tensor", "achieved_ms": round(ms, 5),
+                     "target_ms": round(target, 5), "frac": round(target / ms, 4),
+                     "nvlink_bytes_received_per_rank": recv, "nvlink_gbs_ref": nvlink_gbs,
+                     "gemm_floor_ms": round(t_gemm, 5), "link_floor_ms": round(t_link, 5),
+                     "note": "fused compute+collective: target = max(ops / measured INT8 peak, bytes each rank "
+                             "receives / 770 GB/s measured peer bandwidth)"},
+        "cpu_baseline": None,
+        "e2e": {"value": round(2.0 * M * N * K / (e2e_ms * 1e-3) / 1e12, 3), "unit": UNIT,
+                "h2d_bytes_per_step": M * K * 2 * world, "d2h_bytes_per_step": M * N * 2,
+                "api": "rdna2_ops.w8a8_linear on each rank's shard (C ABI b2_quant_linear); pinned host X to "
+                       "every GPU, each rank's N/P columns back over its own PCIe link; uploads / linear / "
+                       "read-backs on three streams, double buffered",
+                "ms_per_step": round(e2e_ms, 4)},
+        "gpu_launches": 3 * args.steps,
+        "clocks": clocks.summary(),
+        "device_status": status,
+        "wall_s_timed": round(t_wall, 4),
+        "side": {
+            "local_linear_only_ms": round(local_ms, 5),
+            "local_linear_only_tops": round(world * 2.0 * M * ns * K / (local_ms * 1e-3) / 1e12, 2),
+            "nccl_allgather_step_ms": round(nccl_ms, 5),
+            "nccl_allgather_step_tops": round(2.0 * M * N * K / (nccl_ms * 1e-3) / 1e12, 2),
+            "nccl_note": "local linear + all_gather_into_tensor into [P*M, N/P] (no permute), serial",
+            "weak_ms": round(weak_ms, 5),
+            "weak_tops": round(world * 2.0 * M * N * K / (weak_ms * 1e-3) / 1e12, 2),
+            "weak_note": "12288 columns per rank of a 12288*P-column layer, fused gather inside the step",
+        },
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_c5_multi(args, rank, world, local_rank):
+    """Config 5 on P GPUs: the 28-block DiT linear stack column-parallel, every
+    layer output reassembled on every rank inside the GEMM epilogue (fused
+    gather) before the next linear reads it.  One step = the whole stack."""
+    import torch
+    import torch.distributed as dist
+    from rdna2_ops import _native as nat
+    from rdna2_ops import qlinear
+    from rdna2_ops.column_parallel import ColumnParallelStack, PeerGather
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED)
+    m, hid, nblocks = 8192, 3072, 28
+    shapes = ((3 * hid, hid), (hid, hid), (4 * hid, hid), (hid, 4 * hid))
+    blocks = []
+    for _ in range(nblocks):
+        blk = []
+        for n_, k_ in shapes:
+            w = torch.randn((n_, k_), generator=gen, device=dev) * (1.0 / k_ ** 0.5)
+            blk.append(qlinear.quantize_weight(w, rotation_block=ROT))
+            del w
+        blocks.append(blk)
+    x0 = torch.randn((m, hid), generator=gen, device=dev).half()
+    g = PeerGather(m * 4 * hid, torch.float16)
+    stack = ColumnParallelStack(blocks, peers=g, gather="peer")
+    del blocks
+    torch.cuda.empty_cache()
+
+    def barrier():
+        dist.barrier(device_ids=[local_rank])
+
+    for _ in range(max(3, args.warmup)):
+        y = stack(x0)
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(y).all()), "stack output not finite"
+    nat.device_status(reset=True)
+    steps = max(3, min(args.steps, 30))
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        e0.record(stream)
+        for _ in range(steps):
+            stack(x0)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = _max_over_ranks(torch, dist, dev, e0.elapsed_time(e1) / steps)
+    status = nat.device_status()
+    g.close()
+    if rank != 0:
+        return
+    flops = 2.0 * m * sum(n_ * k_ for n_, k_ in shapes) * nblocks
+    recv = (world - 1) / world * m * sum(n_ for n_, _ in shapes) * 2 * nblocks
+    line = {"workload": "c5", "metric": "W8A8 DiT stack TOPS (config 5, 28 blocks, rotated)",
+            "value": round(flops / (ms * 1e-3) / 1e12, 2), "unit": "TOPS", "n_gpus": world, "steps": steps,
+            "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "strong", "dtype": "int8", "data": "synthetic",
+            "config": {"M": m, "hidden": hid, "blocks": nblocks,
+                       "linears": "QKV 9216x3072, out 3072x3072 (on the Q third), up 12288x3072, down 3072x12288, "
+                                  "block-128 rotation, every weight N-sharded over the ranks",
+                       "parallelism": f"column-parallel x{world}, every layer output gathered to every rank "
+                                      "inside the GEMM epilogue (NVLink peer stores)"},
+            "roofline": {"bound": "nvlink", "nvlink_bytes_received_per_rank": int(recv),
+                         "link_floor_ms": round(recv / 770e9 * 1e3, 3),
+                         "gemm_floor_ms": round(flops / world / (2.0 * peaks()["bf16_tflops"] * 1e12) * 1e3, 3),
+                         "frac": round(max(recv / 770e9 * 1e3,
+                                           flops / world / (2.0 * peaks()["bf16_tflops"] * 1e12) * 1e3) / ms, 4)},
+            "gpu_launches": 3 * 4 * nblocks * steps, "clocks": clocks.summary(), "device_status": status,
+            "timing": "eager public ColumnParallelStack calls"}
     print(json.dumps(line), flush=True)
 
 
@@ -726,7 +1054,7 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank)
         return
-    if args.workload != "c2":
+    if args.workload not in ("c2", "c5") or (args.workload == "c5" and world == 1):
         if rank == 0:
             run_workload(args)
         return
@@ -738,7 +1066,12 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_b200(args, rank, world, local_rank)
+        if world > 1 and args.workload == "c5":
+            run_c5_multi(args, rank, world, local_rank)
+        elif world > 1:
+            run_b200_multi(args, rank, world, local_rank)
+        else:
+            run_b200(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -223,6 +223,52 @@ int b2_unpack_int4(const void* data, int layout_kn, int order_high, const float*
                    const void* zeros, int64_t N, int64_t K, int group, int out_dtype, void* out,
                    void* stream);
 
+/* ---- Column-parallel linear with the output gather fused into the GEMM ----
+ * One process per GPU; the weight is N-sharded across `world` ranks and every
+ * rank holds a full output buffer Y[M, ldc] plus a gather-state buffer of
+ * b2_gather_state_bytes() bytes (256-byte aligned, zero-filled once before
+ * first use).  Each rank maps its peers' output and state buffers into its own
+ * address space with the IPC helpers below.  Replaces the multi-GPU
+ * reassembly of the per-layer linear production/MOSS_RDNA2_INT8/backend.py
+ * :112-145 (the reference itself is single-GPU), i.e. ColumnParallelLinear's
+ * NCCL all-gather of the shard outputs.
+ *
+ * b2_ipc_export: handle (b2_ipc_handle_bytes() bytes) and byte offset of the
+ *   device allocation holding `ptr` (cudaIpcGetMemHandle of its base).
+ * b2_ipc_import: map a peer's exported allocation into this process (peer
+ *   access enabled lazily); *ptr = mapped base + offset.  Reference counted per
+ *   handle; b2_ipc_release drops one reference and unmaps at zero. */
+size_t b2_ipc_handle_bytes(void);
+int b2_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+int b2_ipc_import(const void* handle, uint64_t offset, void** ptr);
+int b2_ipc_release(const void* handle);
+size_t b2_gather_state_bytes(void);
+
+/* The fused linear of b2_quant_linear for this rank's shard (w [N,K], w_scale,
+ * bias: the shard's rows), with the epilogue writing each output tile into
+ * columns [col0, col0 + N) of EVERY rank's output: outs[r] = rank r's full
+ * output buffer as mapped here (outs[rank] the local one), states[r] = rank
+ * r's gather-state buffer as mapped here.  Peer copies are plain 16-byte
+ * stores over NVLink issued while later tiles are still being multiplied.
+ * When all of this rank's work is stored, `epoch` (nonzero, increasing per
+ * call) is released into slot `rank` of every rank's state.  Requires
+ * N % 64 == 0, 16-byte aligned output rows and columns (col0, ldc), kind 0/1.
+ * M == 0 launches nothing and releases nothing.  Output buffers are written by
+ * every rank: a consumer may read Y only after b2_gather_wait for the epoch,
+ * and a rank may start the next call writing the same buffer only after every
+ * rank has finished reading it (alternate two buffers between layers). */
+int b2_quant_linear_gather(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
+                           const void* w, int64_t ldw, int64_t N, const float* w_scale, int64_t w_scale_count,
+                           const void* bias, int bias_dtype, int epilogue, int out_dtype, int64_t ldc,
+                           int64_t col0, int world, int rank, void* const* outs, void* const* states,
+                           uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Enqueue a wait (one small kernel) until every one of the `world` slots of
+ * the LOCAL gather state holds `epoch` or later, i.e. every rank's shard of
+ * that call has landed in the local output buffer.  Bounded: after 2 s the
+ * kernel gives up and sets b2_device_status to 0x107. */
+int b2_gather_wait(const void* state, int world, uint32_t epoch, void* stream);
+
 /* Allocation-free fused quantized linear: the same computation and results
  * as b2_quant_linear, for callers that cannot provide a workspace (a host
  * whose device memory is all owned by another allocator, a plugin calling

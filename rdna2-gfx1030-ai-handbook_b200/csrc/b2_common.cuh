@@ -26,6 +26,7 @@ enum : int {
   kSiteEpilogue = 4,
   kSiteTransform = 5,
   kSiteFixup = 6,
+  kSiteGather = 7,
 };
 
 // Longest time any single mbarrier wait may take before the CTA abandons its
@@ -411,6 +412,24 @@ __device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
                : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]),
                  "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]),
                  "+r"(r[13]), "+r"(r[14]), "+r"(r[15])::"memory");
+}
+
+// ------------------------------------------------- peer (NVLink) memory
+// Plain 16-byte store; with a peer pointer it travels over NVLink.  Never a
+// TMA or bulk copy on peer memory.
+__device__ __forceinline__ void st_global_v4(void* ptr, uint4 v) {
+  asm volatile("st.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(ptr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* ptr) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {

@@ -6,6 +6,9 @@
 
 namespace b2 {
 
+// Most peers one column-parallel gather writes to (8 GPUs per node).
+constexpr int kMaxGatherPeers = 7;
+
 struct GemmParams {
   int M, N, K;
   int tiles_m, tiles_n, num_kb;
@@ -25,7 +28,29 @@ struct GemmParams {
   // kernel (its own activation prologue) never writes the weights; any other
   // caller's previous kernel may, and its writes are visible only after the wait.
   int weight_prefetch;
+  // Column-parallel output gather (b2_quant_linear_gather; pair TMA-store
+  // kernel only).  Besides its TMA store of `out`, the epilogue writes every
+  // staged 32-row x 128-byte output unit to the n_peers buffers peer_out[i]
+  // (other GPUs' full outputs, mapped into this process and offset to this
+  // rank's columns; row stride ldc) with plain 16-byte stores over NVLink.
+  // The last CTA to finish (counted in *done_count, which it leaves at zero)
+  // then stores `epoch` with release semantics at system scope into each of
+  // flag_slot[0..n_peers] -- this rank's slot in every rank's flag array, its
+  // own included -- after a system-scope fence in every epilogue thread.
+  int gather;
+  int n_peers;
+  void* peer_out[kMaxGatherPeers];
+  uint32_t* flag_slot[kMaxGatherPeers + 1];
+  uint32_t* done_count;
+  uint32_t epoch;
 };
+
+// Argument check of the fused linear (b2_quant_linear): 0 when valid,
+// including every M == 0 or N == 0 call; the gather variant shares it.
+int check_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
+                       const void* w, int64_t ldw, int64_t N, const float* w_scale, int64_t w_scale_count,
+                       const void* bias, int bias_dtype, int epilogue, const void* out, int out_dtype,
+                       int64_t ldc, const void* workspace, size_t workspace_bytes);
 
 // Device address of the bounded-wait status word on the current device.
 int* status_word_ptr();

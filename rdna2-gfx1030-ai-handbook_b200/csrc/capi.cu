@@ -133,11 +133,14 @@ size_t b2_quant_linear_workspace_bytes(int64_t M, int64_t K) {
   return static_cast<size_t>(round_up(M * round_up(K, 16), 256) + round_up(M * 4, 256));
 }
 
-int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
-                    const void* w, int64_t ldw, int64_t N, const float* w_scale,
-                    int64_t w_scale_count, const void* bias, int bias_dtype, int epilogue, void* out,
-                    int out_dtype, int64_t ldc, void* workspace, size_t workspace_bytes,
-                    void* stream) {
+}  // extern "C"
+
+// Argument check of the fused linear (shared with the gather variant):
+// 0 when the call is valid, including every M == 0 or N == 0 call.
+int b2::check_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
+                           const void* w, int64_t ldw, int64_t N, const float* w_scale, int64_t w_scale_count,
+                           const void* bias, int bias_dtype, int epilogue, const void* out, int out_dtype,
+                           int64_t ldc, const void* workspace, size_t workspace_bytes) {
   if (kind != b2::kKindI8 && kind != b2::kKindE4M3) return fail();
   if (epilogue == b2::kEpiNone) return fail();
   if (M < 0 || K < 1 || K > 16384 || x_dtype < 0 || x_dtype > 2 || !valid_block(block, K)) return fail();
@@ -149,6 +152,20 @@ int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, 
   if (!x || ldx < K) return fail();
   if (reinterpret_cast<uintptr_t>(workspace) % 256 != 0) return fail();
   if (workspace_bytes < b2_quant_linear_workspace_bytes(M, K)) return fail();
+  return 0;
+}
+
+extern "C" {
+
+int b2_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
+                    const void* w, int64_t ldw, int64_t N, const float* w_scale,
+                    int64_t w_scale_count, const void* bias, int bias_dtype, int epilogue, void* out,
+                    int out_dtype, int64_t ldc, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  int st = b2::check_quant_linear(kind, x, x_dtype, M, K, ldx, block, w, ldw, N, w_scale, w_scale_count, bias,
+                                  bias_dtype, epilogue, out, out_dtype, ldc, workspace, workspace_bytes);
+  if (st != 0 || M == 0 || N == 0) return st;
+  const int64_t ldq = round_up(K, 16);
   uint8_t* q = static_cast<uint8_t*>(workspace);
   float* sa = reinterpret_cast<float*>(q + round_up(M * ldq, 256));
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -1,0 +1,201 @@
+// Column-parallel fused linear with the output all-gather folded into the
+// GEMM (one process per GPU, weights N-sharded across the ranks of a node).
+//
+// Each rank computes its N-shard of Y = epilogue(quantize(rotate(x)) @ W.T)
+// with the pair TMA-store GEMM, whose epilogue writes every finished output
+// unit both to its own full output buffer (TMA store) and, with plain 16-byte
+// stores over NVLink, into the same columns of every peer's full output
+// buffer.  The transfer therefore overlaps the MMAs tile by tile, and every
+// rank ends with the whole row-major Y[M, N_total] -- no separate collective
+// and no permute pass.  Completion is signalled per rank through a small
+// "gather state" buffer on every GPU: rank r's GEMM releases an epoch number
+// into slot r of every rank's flag array once all of its CTAs are done, and
+// b2_gather_wait (one tiny kernel) acquires all slots of the local array
+// before the stream moves on.  All waits are bounded.
+//
+// Peer buffers are reached through CUDA IPC (b2_ipc_export / b2_ipc_import);
+// no TMA, bulk copy or multicast ever touches peer memory.
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+
+#include "../../include/b2_qlinear.h"
+#include "b2_common.cuh"
+#include "b2_internal.h"
+
+namespace {
+
+constexpr int kStateBytes = 256;        // flags [0, 32) bytes, counter at 128
+constexpr int kCounterOffset = 128;
+
+inline int fail() { return static_cast<int>(cudaErrorInvalidValue); }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+typedef CUresult (*AddressRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+AddressRangeFn address_range() {
+  static AddressRangeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<AddressRangeFn>(ptr);
+  });
+  return fn;
+}
+
+// Opened IPC mappings of this process, by handle bytes: one open per
+// allocation (a second cudaIpcOpenMemHandle of the same handle fails).
+struct Mapping {
+  void* base = nullptr;
+  int refs = 0;
+};
+std::mutex g_ipc_mutex;
+std::map<std::string, Mapping> g_mappings;
+
+__global__ void gather_wait_kernel(const uint32_t* flags, int world, uint32_t epoch, int* status) {
+  const int r = static_cast<int>(threadIdx.x);
+  if (r >= world) return;
+  const uint64_t start = b2::globaltimer();
+  for (uint32_t i = 0;; ++i) {
+    const uint32_t v = b2::ld_acquire_sys(flags + r);
+    if (static_cast<int32_t>(v - epoch) >= 0) return;  // this epoch or a later one
+    if ((i & 255u) == 255u && b2::globaltimer() - start > b2::kWaitLimitNs) {
+      if (status != nullptr) atomicCAS(status, 0, 0x100 | b2::kSiteGather);
+      return;
+    }
+    __nanosleep(100);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t b2_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+int b2_ipc_export(const void* ptr, void* handle, uint64_t* offset) {
+  if (!ptr || !handle || !offset) return fail();
+  AddressRangeFn fn = address_range();
+  if (fn == nullptr) return static_cast<int>(cudaErrorNotSupported);
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(ptr)) != CUDA_SUCCESS) return fail();
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+  if (e != cudaSuccess) return static_cast<int>(e);
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<uint64_t>(reinterpret_cast<uintptr_t>(ptr) - static_cast<uintptr_t>(base));
+  return 0;
+}
+
+int b2_ipc_import(const void* handle, uint64_t offset, void** ptr) {
+  if (!handle || !ptr) return fail();
+  const std::string key(static_cast<const char*>(handle), sizeof(cudaIpcMemHandle_t));
+  std::lock_guard<std::mutex> lock(g_ipc_mutex);
+  Mapping& m = g_mappings[key];
+  if (m.refs == 0) {
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      g_mappings.erase(key);
+      return static_cast<int>(e);
+    }
+    m.base = base;
+  }
+  ++m.refs;
+  *ptr = static_cast<char*>(m.base) + offset;
+  return 0;
+}
+
+int b2_ipc_release(const void* handle) {
+  if (!handle) return fail();
+  const std::string key(static_cast<const char*>(handle), sizeof(cudaIpcMemHandle_t));
+  std::lock_guard<std::mutex> lock(g_ipc_mutex);
+  auto it = g_mappings.find(key);
+  if (it == g_mappings.end()) return fail();
+  if (--it->second.refs == 0) {
+    cudaError_t e = cudaIpcCloseMemHandle(it->second.base);
+    g_mappings.erase(it);
+    return static_cast<int>(e);
+  }
+  return 0;
+}
+
+size_t b2_gather_state_bytes(void) { return kStateBytes; }
+
+int b2_gather_wait(const void* state, int world, uint32_t epoch, void* stream) {
+  if (!state || world < 1 || world > b2::kMaxGatherPeers + 1 || epoch == 0) return fail();
+  if (reinterpret_cast<uintptr_t>(state) % 256 != 0) return fail();
+  gather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint32_t*>(state), world, epoch, b2::status_word_ptr());
+  return static_cast<int>(cudaGetLastError());
+}
+
+int b2_quant_linear_gather(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
+                           const void* w, int64_t ldw, int64_t N, const float* w_scale, int64_t w_scale_count,
+                           const void* bias, int bias_dtype, int epilogue, int out_dtype, int64_t ldc,
+                           int64_t col0, int world, int rank, void* const* outs, void* const* states,
+                           uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
+  if (world < 1 || world > b2::kMaxGatherPeers + 1 || rank < 0 || rank >= world) return fail();
+  if (!outs || !states || epoch == 0) return fail();
+  if (out_dtype != b2::kF16 && out_dtype != b2::kBF16 && out_dtype != b2::kF32) return fail();
+  const int ob = out_dtype == b2::kF32 ? 4 : 2;
+  if (N % 64 != 0 || col0 < 0 || col0 + N > ldc || (col0 * ob) % 16 != 0 || (ldc * ob) % 16 != 0) return fail();
+  for (int q = 0; q < world; ++q) {
+    if (!outs[q] || !aligned16(outs[q]) || !states[q]) return fail();
+    if (reinterpret_cast<uintptr_t>(states[q]) % 256 != 0) return fail();
+  }
+  char* own = static_cast<char*>(outs[rank]) + col0 * ob;
+  // The fused linear's own argument check, with this rank's columns of its
+  // own output as `out`.  M == 0 launches nothing and releases no flag, so
+  // callers skip b2_gather_wait for it too.
+  int st = b2::check_quant_linear(kind, x, x_dtype, M, K, ldx, block, w, ldw, N, w_scale, w_scale_count, bias,
+                                  bias_dtype, epilogue, own, out_dtype, ldc, workspace, workspace_bytes);
+  if (st != 0 || M == 0) return st;
+  const int64_t ldq = round_up(K, 16);
+  uint8_t* q = static_cast<uint8_t*>(workspace);
+  float* sa = reinterpret_cast<float*>(q + round_up(M * ldq, 256));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = b2::run_act_quant(x, x_dtype, M, K, ldx, block, kind == b2::kKindE4M3 ? 1 : 0, q, ldq, sa, s,
+                                    /*early_dependents=*/true);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  b2::GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.sa = sa;
+  p.sb = w_scale;
+  p.sb_scalar = w_scale_count == 1 ? 1 : 0;
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.out = own;
+  p.out_dtype = out_dtype;
+  p.ldc = ldc;
+  p.epilogue = epilogue;
+  p.vec_ok = 1;
+  p.weight_prefetch = 1;
+  p.gather = 1;
+  p.n_peers = 0;
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    p.peer_out[p.n_peers++] = static_cast<char*>(outs[r]) + col0 * ob;
+  }
+  int slot = 0;
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    p.flag_slot[slot++] = static_cast<uint32_t*>(states[r]) + rank;
+  }
+  p.flag_slot[slot] = static_cast<uint32_t*>(states[rank]) + rank;
+  p.done_count = reinterpret_cast<uint32_t*>(static_cast<char*>(states[rank]) + kCounterOffset);
+  p.epoch = epoch;
+  return static_cast<int>(b2::run_qgemm(kind, q, ldq, w, ldw, p, 0, s));
+}
+
+}  // extern "C"

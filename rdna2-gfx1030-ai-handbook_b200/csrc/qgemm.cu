@@ -320,13 +320,53 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tadd
   }
 }
 
+// Column-parallel gather: copy one staged unit (32 rows x 128 bytes at
+// `buf`, 128-byte swizzle) to every peer output with 16-byte stores, four
+// whole 128-byte row segments per warp instruction.  Gather mode requires
+// N % 64 == 0 and 16-byte aligned output rows, so a piece is either wholly
+// inside the output or wholly past it.
+__device__ __forceinline__ void peer_store_unit(const GemmParams& p, uint32_t buf, int row0, int x, int lane) {
+  const int ob = (p.out_dtype == kF16 || p.out_dtype == kBF16) ? 2 : 4;
+  const int j = lane & 7;
+  if (x + j * (16 / ob) >= p.N) return;
+#pragma unroll 2
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + (lane >> 3);
+    const uint4 v = lds_v4(buf + static_cast<uint32_t>(r * 128) + (static_cast<uint32_t>(j ^ (r & 7)) << 4));
+    if (row0 + r < p.M) {
+      const int64_t off = (static_cast<int64_t>(row0 + r) * p.ldc + x) * ob + j * 16;
+      for (int q = 0; q < p.n_peers; ++q) st_global_v4(static_cast<char*>(p.peer_out[q]) + off, v);
+    }
+  }
+}
+
+// End of a gather-mode kernel, run by all epilogue threads of every CTA:
+// each orders its peer stores before a CTA-wide barrier with a system-scope
+// fence; one thread per CTA counts the CTA; the last CTA fences again and
+// releases `epoch` into every flag slot (the peers' arrays and its own), then
+// rearms the counter for the next launch on the stream.
+constexpr int kGatherBarrier = 2;
+
+__device__ __forceinline__ void gather_signal(const GemmParams& p) {
+  __threadfence_system();
+  named_bar_sync(kGatherBarrier, kEpiWarps * 32);
+  if (threadIdx.x == 64) {  // first epilogue thread
+    const uint32_t prev = atomicAdd(p.done_count, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int q = 0; q <= p.n_peers; ++q) st_release_sys(p.flag_slot[q], p.epoch);
+      *p.done_count = 0u;
+    }
+  }
+}
+
 // The same epilogue with the output staged through shared memory: each
 // 128-byte-wide column unit of the warp's 32 rows is written into one of two
 // swizzled staging buffers and leaves as one TMA store (whole 128-byte lines
 // to L2 instead of 32 half-sector stores per instruction), while the next
 // unit is converted.  Lane 0 issues and waits on the warp's bulk groups; the
 // tensor map clips rows >= M and columns >= N.
-template <int KIND, int BN, typename Release>
+template <int KIND, int BN, bool GATHER, typename Release>
 __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const CUtensorMap* tma_c, uint32_t taddr,
                                                   int row, int row0, int n0, int lane, float* wst,
                                                   uint32_t obuf, uint32_t& ob_sel, Release release) {
@@ -351,6 +391,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const CUt
         tma_store_2d(tma_c, buf, x, row0);
         bulk_commit_group();
       }
+      if constexpr (GATHER) peer_store_unit(p, buf, row0, x, lane);
       ob_sel ^= 1u;
     }
   };
@@ -548,7 +589,7 @@ __global__ void __launch_bounds__(192, 1)
 // and signals both CTAs' `empty` / `tfull` barriers with one commit each;
 // both epilogues hand TMEM back through the leader's `tempty` barrier (8
 // arrivals).
-template <int KIND, int BN, int STAGES, bool TSTORE>
+template <int KIND, int BN, int STAGES, bool TSTORE, bool GATHER = false>
 __global__ void __launch_bounds__(192, 1)
     qgemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                       const __grid_constant__ CUtensorMap tma_b,
@@ -703,8 +744,8 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) mbar_arrive_cluster(tempty_leader + static_cast<uint32_t>(buf * 8));
       };
       if constexpr (TSTORE) {
-        epilogue_tile_tma<KIND, BN>(p, &tma_c, taddr, row0 + lane, row0, tn * BN, lane, wsb, obuf, ob_sel,
-                                    release);
+        epilogue_tile_tma<KIND, BN, GATHER>(p, &tma_c, taddr, row0 + lane, row0, tn * BN, lane, wsb, obuf,
+                                            ob_sel, release);
       } else {
         epilogue_tile<KIND, BN>(p, taddr, row0 + lane, tn * BN, lane, wsb, release);
       }
@@ -713,6 +754,7 @@ __global__ void __launch_bounds__(192, 1)
       if (lane == 0) bulk_wait_all();  // staging reads and global writes done
       __syncwarp();
     }
+    if constexpr (GATHER) gather_signal(p);
   }
 
   tc_fence_before();
@@ -1098,11 +1140,11 @@ static cudaError_t launch_single(const void* a, int64_t lda, const void* b, int6
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
-template <int KIND, int BN, int STAGES, bool TSTORE>
+template <int KIND, int BN, int STAGES, bool TSTORE, bool GATHER = false>
 static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams p,
                                int max_ctas, cudaStream_t stream) {
   using L = Smem<128, BN / 2, BN, STAGES, TSTORE ? kOutStageBytes : 0>;
-  auto kernel = qgemm_pair_kernel<KIND, BN, STAGES, TSTORE>;
+  auto kernel = qgemm_pair_kernel<KIND, BN, STAGES, TSTORE, GATHER>;
   static bool configured[64] = {false};
   static int max_pairs[64] = {0};
   cudaError_t e = configure_once(kernel, L::kAlloc, configured);
@@ -1286,6 +1328,27 @@ static cudaError_t dispatch(int cfg, const void* a, int64_t lda, const void* b, 
   }
 }
 
+// Gather mode: the pair TMA-store kernel with peer stores, 256x256 or
+// 256x192 tiles by the same wave model as the automatic choice.
+static cudaError_t run_gather(int kind, const void* a, int64_t lda, const void* b, int64_t ldb,
+                              const GemmParams& p, cudaStream_t stream) {
+  if (!p.vec_ok || p.N % 64 != 0 || p.n_peers < 0 || p.n_peers > kMaxGatherPeers || !p.done_count)
+    return cudaErrorInvalidValue;
+  const int pairs = pair_capacity();
+  if (pairs <= 0) return cudaErrorNotSupported;
+  const int64_t tm2 = (p.M + 255) / 256;
+  const int64_t w256 = (tm2 * ((p.N + 255) / 256) + pairs - 1) / pairs;
+  const int64_t w192 = (tm2 * ((p.N + 191) / 192) + pairs - 1) / pairs;
+  const bool narrow = static_cast<double>(w192) * 192.0 * 1.06 < static_cast<double>(w256) * 256.0;
+  if (kind == kKindI8)
+    return narrow ? launch_pair<kKindI8, 192, 6, true, true>(a, lda, b, ldb, p, 0, stream)
+                  : launch_pair<kKindI8, 256, 6, true, true>(a, lda, b, ldb, p, 0, stream);
+  if (kind == kKindE4M3)
+    return narrow ? launch_pair<kKindE4M3, 192, 6, true, true>(a, lda, b, ldb, p, 0, stream)
+                  : launch_pair<kKindE4M3, 256, 6, true, true>(a, lda, b, ldb, p, 0, stream);
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, GemmParams p,
                       int max_ctas, cudaStream_t stream) {
   if (p.M == 0 || p.N == 0) return cudaSuccess;
@@ -1293,6 +1356,7 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
   const int eb = (kind == kKindBF16 || kind == kKindF16) ? 2 : 1;
   const int kb_elems = 128 / eb;
   p.num_kb = static_cast<int>((p.K + kb_elems - 1) / kb_elems);
+  if (p.gather) return run_gather(kind, a, lda, b, ldb, p, stream);
   int cfg = g_force_path;
   const int64_t tm = (p.M + 127) / 128;
   const bool wide = p.N > 128 && tm * ((p.N + 255) / 256) >= device_sm_count() / 2;

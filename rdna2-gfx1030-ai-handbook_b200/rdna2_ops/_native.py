@@ -57,6 +57,15 @@ SIGNATURES = {
     "b2_fp8_decode": ([_p, _int, _i64, _i64, _i64, _int, _p, _i64, _p], _int),
     "b2_pack_int4": ([_p, _int, _i64, _i64, _i64, _int, _int, _int, _int, _p, _p, _p, _p, _p], _int),
     "b2_unpack_int4": ([_p, _int, _int, _p, _p, _i64, _i64, _int, _int, _p, _p], _int),
+    "b2_ipc_handle_bytes": ([], _size),
+    "b2_ipc_export": ([_p, _p, ctypes.POINTER(ctypes.c_uint64)], _int),
+    "b2_ipc_import": ([_p, ctypes.c_uint64, ctypes.POINTER(_p)], _int),
+    "b2_ipc_release": ([_p], _int),
+    "b2_gather_state_bytes": ([], _size),
+    "b2_quant_linear_gather": ([_int, _p, _int, _i64, _i64, _i64, _int, _p, _i64, _i64, _p, _i64, _p, _int,
+                                _int, _int, _i64, _i64, _int, _int, ctypes.POINTER(_p), ctypes.POINTER(_p),
+                                ctypes.c_uint32, _p, _size, _p], _int),
+    "b2_gather_wait": ([_p, _int, ctypes.c_uint32, _p], _int),
     "b2_quant_linear_noalloc_max_bytes": ([], _size),
     "b2_quant_linear_noalloc": ([_int, _p, _int, _i64, _i64, _i64, _int, _p, _i64, _i64, _p, _i64,
                                  _p, _int, _int, _p, _int, _i64, _p], _int),

@@ -143,3 +143,77 @@ def test_nccl_column_parallel_bit_identical():
         p.join(300)
         assert p.exitcode == 0
     assert all(ok for _, ok in sorted(q.get(timeout=10) for _ in range(2)))
+
+
+def _peer_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    g = None
+    try:
+        from rdna2_ops import qlinear, w8a8_linear
+        from rdna2_ops.column_parallel import ColumnParallelStack, PeerGather
+        gen = torch.Generator(device="cuda").manual_seed(20261106)
+        m, n, k = 1000, 768 * world, 3072
+        x = torch.randn((m, k), generator=gen, device="cuda").half()
+        w = torch.randn((n, k), generator=gen, device="cuda") * 0.02
+        wq, sw = qlinear.quantize_weight(w, rotation_block=128)
+        bias = (torch.randn(n, generator=gen, device="cuda") * 0.02).half()
+        g = PeerGather(8192 * 2048, torch.float16)
+        layer = ColumnParallelLinear.from_full(wq, sw, bias, rotation_block=128, out_dtype=torch.float16,
+                                               gather="peer", peers=g)
+        ref = w8a8_linear(x, wq, sw, bias, rotation_block=128, out_dtype=torch.float16)
+        ok = True
+        for _ in range(5):                      # both ring buffers, several epochs
+            y = layer(x)
+            ok &= bool(torch.equal(y.view(torch.int16), ref.view(torch.int16)))
+        # two DiT blocks (hidden 512), column-parallel with the peer gather,
+        # against the same chain of single-GPU fused linears
+        hid, blocks = 512, []
+        for _ in range(2):
+            blk = []
+            for nn_, kk in ((3 * hid, hid), (hid, hid), (4 * hid, hid), (hid, 4 * hid)):
+                wf = torch.randn((nn_, kk), generator=gen, device="cuda") / kk ** 0.5
+                blk.append(qlinear.quantize_weight(wf, rotation_block=128))
+            blocks.append(blk)
+        x0 = torch.randn((256, hid), generator=gen, device="cuda").half()
+        yr = x0
+        for blk in blocks:
+            (q1, s1), (q2, s2), (q3, s3), (q4, s4) = blk
+            qkv = w8a8_linear(yr, q1, s1, rotation_block=128, out_dtype=torch.float16)
+            o = w8a8_linear(qkv[:, :hid], q2, s2, rotation_block=128, out_dtype=torch.float16)
+            yr = w8a8_linear(w8a8_linear(o, q3, s3, rotation_block=128, out_dtype=torch.float16), q4, s4,
+                             rotation_block=128, out_dtype=torch.float16)
+        stack = ColumnParallelStack(blocks, peers=g, gather="peer")
+        ys = stack(x0)
+        ok_stack = bool(torch.equal(ys.view(torch.int16), yr.view(torch.int16)))
+        from rdna2_ops import _native as nat
+        q.put((rank, ok, ok_stack, nat.device_status()))
+    finally:
+        if g is not None:
+            g.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_peer_gather_column_parallel_bit_identical():
+    """Every rank's reassembled output (the gather inside the GEMM epilogue,
+    over NVLink) equals the single-GPU fused linear bit for bit, over several
+    epochs; a 2-block column-parallel DiT stack equals the 1-GPU stack."""
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    res = sorted(q.get(timeout=10) for _ in range(world))
+    assert all(ok and ok_stack and st == 0 for _, ok, ok_stack, st in res), res
