@@ -56,8 +56,9 @@ def parse():
     ap.add_argument("--sets", type=int, default=4, help="input sets cycled to defeat L2 reuse")
     ap.add_argument("--workload", default="c2",
                     help="c2 (headline, default), c1, c3m1/c3m16/c3m128/c3m2048 (W4A16), "
-                         "c4m1/c4m2048 (FP8), w4a8m<M> (W4A8), c5 (28-block W8A8 DiT stack); "
-                         "non-c2 workloads run on one GPU")
+                         "c4m1/c4m2048 (FP8), w4a8m<M> (W4A8), c5 (28-block W8A8 DiT stack; also "
+                         "column-parallel under torchrun), moss (the reference's four M=1061 shapes); "
+                         "other workloads run on one GPU")
     return ap.parse_args()
 
 
@@ -631,6 +632,31 @@ def run_b200_multi(args, rank, world, local_rank):
         nccl(i)
     nccl_ms, _, _ = timed(nccl, n_side)
     del gathered
+    # link bandwidth in this run: every rank copies its [M, N/P] block into the
+    # same columns of every peer's full output with the copy engines (one 2-D
+    # copy per peer, each on its own stream) -- the gather's traffic without
+    # the GEMM
+    slot = 0
+    peer_streams = [torch.cuda.Stream(dev) for _ in range(world - 1)]
+    src_ptr = g.outs[slot][rank] + c0 * 2
+
+    def ce_gather(i):
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        j = 0
+        for q in range(world):
+            if q == rank:
+                continue
+            st_ = peer_streams[j]
+            st_.wait_event(ev)
+            nat.check(lib.b2_peer_copy_2d(g.outs[slot][q] + c0 * 2, N * 2, src_ptr, N * 2, ns * 2, M,
+                                          st_.cuda_stream), "b2_peer_copy_2d")
+            stream.wait_stream(st_)
+            j += 1
+
+    for i in range(3):
+        ce_gather(i)
+    ce_ms, _, _ = timed(ce_gather, max(10, n_side // 4))
     # end to end: X uploaded to every rank, the rank's columns computed by the
     # public call and read back over the rank's own PCIe link; the host holds
     # Y by column shards (no device gather: the consumer is the host)
@@ -705,6 +731,11 @@ def run_b200_multi(args, rank, world, local_rank):
             "weak_ms": round(weak_ms, 5),
             "weak_tops": round(world * 2.0 * M * N * K / (weak_ms * 1e-3) / 1e12, 2),
             "weak_note": "12288 columns per rank of a 12288*P-column layer, fused gather inside the step",
+            "copy_engine_gather_ms": round(ce_ms, 5),
+            "copy_engine_gather_gbs_per_rank": round(recv / (ce_ms * 1e-3) / 1e9, 1),
+            "copy_engine_note": "each rank's [M, N/P] block copied to every peer's Y by 2-D copy-engine "
+                                "copies, one stream per peer, no GEMM: the link bandwidth measured in this run",
+            "fused_gather_gbs_per_rank": round(recv / (ms * 1e-3) / 1e9, 1),
         },
     }
     print(json.dumps(line), flush=True)
@@ -809,6 +840,169 @@ def _raw_linear_step(nat, rdna2_ops, torch, dev, xs, wqs, sw, bias, m, n, k, blo
     torch.cuda.synchronize()
     assert torch.equal(outs[0].view(torch.int16), ref.view(torch.int16)), "raw C-ABI call differs from public call"
     return step, True
+
+
+def torch_cpu_int4_baseline(m, n, k, budget_s, threads):
+    """The reference's PyTorch CPU path for W4A16 (int4_linear_a16 method
+    "dequant": unpack_int4_cpu of the pack, then F.linear in bf16,
+    rdna2_ops/int4_weight_gemm_v07.py:49-92, 540-564) on a bounded row sample."""
+    import torch
+    from rdna2_ops import int4_weight_gemm_v07 as i4
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        g = torch.Generator().manual_seed(SEED)
+        p = i4.pack_int4_cpu(torch.randn((n, k), generator=g) * 0.02, group_size=128, symmetric=False)
+        rows = m
+
+        def run(r):
+            a = torch.randn((r, k), generator=g).to(torch.bfloat16)
+            t0 = time.perf_counter()
+            w = i4.unpack_int4_cpu(p).to(torch.bfloat16)
+            torch.nn.functional.linear(a, w)
+            return time.perf_counter() - t0
+
+        run(1)
+        t1 = run(min(m, 16))
+        if m > 16 and t1 * m / 16 > budget_s:
+            rows = max(16, int(budget_s / t1 * 16) // 16 * 16)
+        dt = min(run(rows), run(rows))
+    finally:
+        torch.set_num_threads(prev)
+    return {"value": round(2.0 * rows * n * k / dt / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"unpack_int4_cpu + F.linear bf16 (method 'dequant') on {rows} of {m} rows, N={n} K={k}, "
+                      f"{dt * 1e3:.1f} ms, {threads} torch threads"}
+
+
+def torch_cpu_fp8_baseline(m, n, k, budget_s, threads):
+    """The reference's PyTorch CPU math for the FP8 weight GEMM (the "upcast"
+    method, F.linear on the decoded weight, rdna2_ops/fp8_weight_gemm_v06.py
+    :166-167) with config 4's scales: per-token e4m3 activations and
+    per-channel e4m3 weights, dequantized to bf16, then F.linear."""
+    import torch
+    prev = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        g = torch.Generator().manual_seed(SEED)
+        w = torch.randn((n, k), generator=g) * 0.02
+        sw = w.abs().amax(1, keepdim=True) / 448.0
+        wq = (w / sw).to(torch.float8_e4m3fn)
+        rows = m
+
+        def run(r):
+            a = torch.randn((r, k), generator=g).to(torch.bfloat16)
+            t0 = time.perf_counter()
+            sa = a.float().abs().amax(1, keepdim=True) / 448.0
+            aq = (a.float() / sa).to(torch.float8_e4m3fn)
+            torch.nn.functional.linear((aq.to(torch.bfloat16) * sa.to(torch.bfloat16)),
+                                       (wq.to(torch.bfloat16) * sw.to(torch.bfloat16)))
+            return time.perf_counter() - t0
+
+        run(1)
+        t1 = run(min(m, 16))
+        if m > 16 and t1 * m / 16 > budget_s:
+            rows = max(16, int(budget_s / t1 * 16) // 16 * 16)
+        dt = min(run(rows), run(rows))
+    finally:
+        torch.set_num_threads(prev)
+    return {"value": round(2.0 * rows * n * k / dt / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"e4m3 per-token / per-channel quantize, dequantize to bf16, F.linear on {rows} of {m} rows, "
+                      f"N={n} K={k}, {dt * 1e3:.1f} ms, {threads} torch threads"}
+
+
+# The reference's measured MOSS linear shapes (M = 1061 tokens) and its
+# published RX 6900 XT times for "fused INT8 GEMM + FP32 dequant" and the
+# row-quantizer + fused GEMM pipeline (rdna2-ops/RDNA2_OPTIMIZATION_GUIDE_KO.md
+# :1135-1138; results/int8_gemm_moss_shapes_v05.json).
+MOSS_SHAPES = ((1061, 3072, 3072, 0.698), (1061, 9216, 3072, 1.869), (1061, 16384, 3072, 3.302),
+               (1061, 3072, 8192, 1.932))
+
+
+def run_moss(args):
+    """One line per MOSS shape: the INT8 GEMM with the fp32 dequant epilogue
+    on pre-quantized operands (int8_gemm_dequant's C-ABI call, b2_qgemm) and
+    the whole linear from fp32 activations (ConvRot 256 + row quantization +
+    GEMM, b2_quant_linear), each a CUDA graph of C-ABI calls with operands
+    cycled over copies larger than L2."""
+    import torch
+    import rdna2_ops
+    from rdna2_ops import _native as nat
+    from rdna2_ops import qlinear
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = nat.library()
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED)
+    stream = torch.cuda.current_stream(dev)
+    pk = peaks()
+    for m, n, k, ref_ms in MOSS_SHAPES:
+        sets = max(4, int(200e6 // (n * k + m * k * 4)) + 1)
+        xs = [torch.randn((m, k), generator=gen, device=dev) for _ in range(sets)]
+        w = torch.randn((n, k), generator=gen, device=dev) * 0.02
+        wq, sw = qlinear.quantize_weight(w, rotation_block=256)
+        del w
+        wqs = [wq.clone() for _ in range(sets)]
+        qa = [rdna2_ops.act_quant(x, rotation_block=256) for x in xs]
+        out = torch.empty((m, n), device=dev, dtype=torch.float32)
+        ws_bytes = lib.b2_quant_linear_workspace_bytes(m, k)
+        ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+        ref = rdna2_ops.int8_gemm_dequant(qa[0][0], wqs[0].T, qa[0][1], sw)
+
+        def gemm(i):
+            j = i % sets
+            nat.check(lib.b2_qgemm(nat.KIND_I8, qa[j][0].data_ptr(), k, wqs[j].data_ptr(), k, m, n, k,
+                                   qa[j][1].data_ptr(), sw.data_ptr(), n, None, 0, nat.EPI_SEPARATE,
+                                   out.data_ptr(), nat.F32, n, stream.cuda_stream), "b2_qgemm")
+
+        def linear(i):
+            j = i % sets
+            nat.check(lib.b2_quant_linear(nat.KIND_I8, xs[j].data_ptr(), nat.F32, m, k, k, 256, wqs[j].data_ptr(),
+                                          k, n, sw.data_ptr(), n, None, 0, nat.EPI_SEPARATE, out.data_ptr(),
+                                          nat.F32, n, ws.data_ptr(), ws_bytes, stream.cuda_stream),
+                      "b2_quant_linear")
+
+        gemm(0)
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int32), ref.view(torch.int32)), "raw GEMM differs from int8_gemm_dequant"
+        times = {}
+        for name, fn in (("gemm", gemm), ("linear", linear)):
+            for i in range(3):
+                fn(i)
+            per = 4 * sets
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(per):
+                    fn(i)
+            graph.replay()
+            torch.cuda.synchronize()
+            reps = max(1, args.steps // per)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(0) as clocks:
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+            times[name] = (e0.elapsed_time(e1) / (reps * per), reps * per, clocks.summary())
+            del graph
+        g_ms, l_ms = times["gemm"][0], times["linear"][0]
+        ops = 2.0 * m * n * k
+        line = {"workload": f"moss m{m} n{n} k{k}", "metric": "INT8 GEMM + FP32 dequant TOPS (MOSS shape)",
+                "value": round(ops / (g_ms * 1e-3) / 1e12, 2), "unit": "TOPS", "n_gpus": 1,
+                "steps": times["gemm"][1], "warmup": 3, "ms_per_step": round(g_ms, 5), "higher_is_better": True,
+                "dtype": "int8", "data": "synthetic",
+                "config": {"M": m, "N": n, "K": k, "out": "fp32", "l2": f"operands cycled over {sets} copies"},
+                "pipeline": {"ms_per_step": round(l_ms, 5), "tops": round(ops / (l_ms * 1e-3) / 1e12, 2),
+                             "what": "fp32 x -> ConvRot 256 + per-token INT8 + GEMM + fp32 dequant (b2_quant_linear)"},
+                "roofline": {"bound": "tensor", "achieved": round(ops / (g_ms * 1e-3) / 1e12, 1),
+                             "peak": round(2.0 * pk["bf16_tflops"], 1), "unit": "TOPS",
+                             "frac": round(ops / (g_ms * 1e-3) / 1e12 / (2.0 * pk["bf16_tflops"]), 4)},
+                "reference_published_ms_rx6900xt": ref_ms,
+                "gpu_launches": times["gemm"][1], "clocks": times["gemm"][2], "timing": "cuda graph of C-ABI calls",
+                "device_status": nat.device_status()}
+        print(json.dumps(line), flush=True)
+        del xs, wqs, qa
 
 
 def run_workload(args):
@@ -1043,6 +1237,11 @@ def run_workload(args):
             "gpu_launches": launches * steps_timed, "clocks": clocks.summary(),
             "timing": "cuda graph of C-ABI calls" if graph_ok else "eager public API calls",
             "device_status": nat.device_status()}
+    if not args.no_cpu_baseline:
+        if name.startswith("c3m"):
+            line["cpu_baseline"] = torch_cpu_int4_baseline(m, n, k, 0.5 * args.cpu_budget_s, host_threads())
+        elif name.startswith("c4m"):
+            line["cpu_baseline"] = torch_cpu_fp8_baseline(m, n, k, 0.5 * args.cpu_budget_s, host_threads())
     print(json.dumps(line), flush=True)
 
 
@@ -1053,6 +1252,10 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.workload == "moss":
+        if rank == 0:
+            run_moss(args)
         return
     if args.workload not in ("c2", "c5") or (args.workload == "c5" and world == 1):
         if rank == 0:

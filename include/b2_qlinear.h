@@ -263,6 +263,13 @@ int b2_quant_linear_gather(int kind, const void* x, int x_dtype, int64_t M, int6
                            int64_t col0, int world, int rank, void* const* outs, void* const* states,
                            uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Copy-engine copy of `rows` rows of `width_bytes` bytes between two device
+ * buffers that may live on different GPUs (an IPC-mapped peer pointer, for
+ * instance): the copy-engine counterpart of the gather, used to measure the
+ * link bandwidth the fused gather is held against.  Asynchronous on `stream`. */
+int b2_peer_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width_bytes, int64_t rows,
+                    void* stream);
+
 /* Enqueue a wait (one small kernel) until every one of the `world` slots of
  * the LOCAL gather state holds `epoch` or later, i.e. every rank's shard of
  * that call has landed in the local output buffer.  Bounded: after 2 s the

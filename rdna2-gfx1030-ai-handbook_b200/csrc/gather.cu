@@ -130,6 +130,15 @@ int b2_ipc_release(const void* handle) {
 
 size_t b2_gather_state_bytes(void) { return kStateBytes; }
 
+int b2_peer_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width_bytes, int64_t rows,
+                    void* stream) {
+  if (!dst || !src || width_bytes < 0 || rows < 0 || dpitch < width_bytes || spitch < width_bytes) return fail();
+  if (width_bytes == 0 || rows == 0) return 0;
+  return static_cast<int>(cudaMemcpy2DAsync(dst, static_cast<size_t>(dpitch), src, static_cast<size_t>(spitch),
+                                            static_cast<size_t>(width_bytes), static_cast<size_t>(rows),
+                                            cudaMemcpyDefault, static_cast<cudaStream_t>(stream)));
+}
+
 int b2_gather_wait(const void* state, int world, uint32_t epoch, void* stream) {
   if (!state || world < 1 || world > b2::kMaxGatherPeers + 1 || epoch == 0) return fail();
   if (reinterpret_cast<uintptr_t>(state) % 256 != 0) return fail();
