@@ -953,13 +953,13 @@ def run_moss(args):
             j = i % sets
             nat.check(lib.b2_qgemm(nat.KIND_I8, qa[j][0].data_ptr(), k, wqs[j].data_ptr(), k, m, n, k,
                                    qa[j][1].data_ptr(), sw.data_ptr(), n, None, 0, nat.EPI_SEPARATE,
-                                   out.data_ptr(), nat.F32, n, stream.cuda_stream), "b2_qgemm")
+                                   out.data_ptr(), nat.F32, n, nat.stream_ptr(dev)), "b2_qgemm")
 
         def linear(i):
             j = i % sets
             nat.check(lib.b2_quant_linear(nat.KIND_I8, xs[j].data_ptr(), nat.F32, m, k, k, 256, wqs[j].data_ptr(),
                                           k, n, sw.data_ptr(), n, None, 0, nat.EPI_SEPARATE, out.data_ptr(),
-                                          nat.F32, n, ws.data_ptr(), ws_bytes, stream.cuda_stream),
+                                          nat.F32, n, ws.data_ptr(), ws_bytes, nat.stream_ptr(dev)),
                       "b2_quant_linear")
 
         gemm(0)
@@ -976,6 +976,9 @@ def run_moss(args):
                     fn(i)
             graph.replay()
             torch.cuda.synchronize()
+            if name == "gemm":   # the replayed graph really computes the product
+                assert torch.equal(out.view(torch.int32), rdna2_ops.int8_gemm_dequant(
+                    qa[(per - 1) % sets][0], wqs[(per - 1) % sets].T, qa[(per - 1) % sets][1], sw).view(torch.int32))
             reps = max(1, args.steps // per)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             with ClockSampler(0) as clocks:

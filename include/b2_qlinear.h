@@ -73,6 +73,13 @@ int b2_set_gemm_path(int path);
  * are identical for every choice.  No reference counterpart. */
 int b2_set_prologue_path(int path);
 
+/* Process-wide W4A16 decode-kernel selection (M <= 32): 0 = automatic (the
+ * kernel that keeps dequantized weights in tensor memory), 1 = the kernel
+ * that stages them in shared memory, 2 = tensor memory.  A tuning and
+ * verification knob: both dequantize identically and differ only in the
+ * tensor core's fp32 summation order.  No reference counterpart. */
+int b2_set_w4a16_path(int path);
+
 /* SYNCHRONOUS: read (and if reset != 0 clear) the device status word that a
  * kernel sets when one of its bounded waits gives up (0 = no failure; else
  * 0x100 | site).  Call after synchronizing the stream. */

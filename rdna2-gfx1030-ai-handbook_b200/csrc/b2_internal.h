@@ -65,6 +65,7 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
 // 0 = automatic, 1 = single-CTA kernel only, 2 = 2-CTA pair kernel only.
 void set_gemm_path(int path);
 void set_prologue_path(int path);
+void set_w4a16_path(int path);
 int pair_capacity();
 
 // Per-row rotate + quantize (quant 0 = int8 /127 RNE, 1 = e4m3 /448, 2 = the

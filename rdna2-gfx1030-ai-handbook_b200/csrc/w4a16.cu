@@ -847,6 +847,363 @@ __global__ void __launch_bounds__(W4DecLayout<BT, RK, RS, NG>::kThreads, 1)
   }
 }
 
+template <int BT, int RK, int RS, int NG, int SA>
+struct W4TmLayout {
+  static constexpr int kAct = BT * 128;
+  static constexpr int kWords = RK * kW4Chunk;
+  static constexpr int kGrp = 2 * RK * kW4GroupBytes;
+  static constexpr int kOffAct = 0;
+  static constexpr int kOffWords = kOffAct + RS * RK * kAct;
+  static constexpr int kOffGrp = kOffWords + RS * kWords;
+  static constexpr int kOffBar = kOffGrp + RS * kGrp;
+  static constexpr int kNumBars = 2 * RS + 2 * NG * SA + 5;
+  static constexpr int kOffMisc = kOffBar + kNumBars * 8;
+  // misc: [0] TMEM base, [4] abort flag
+  static constexpr int kAlloc = kOffMisc + 16 + 1024;
+  static constexpr uint32_t kCols = 2 * NG * BT;       // [buffer][group] accumulators
+  static constexpr uint32_t kSlot0 = (kCols + 31) / 32 * 32;  // [group][SA] dequantized k-blocks, 32 columns each
+  static constexpr uint32_t kTmemCols = 512;
+  static_assert(kSlot0 + NG * SA * 32 <= kTmemCols, "TMEM budget");
+  // warps: producer, NG MMA warps (the first also owns TMEM), NG groups of 4
+  // transform warps, 4 epilogue warps
+  static constexpr int kMmaWarp0 = 1;
+  static constexpr int kXfWarp0 = 1 + NG;
+  static constexpr int kEpiWarp0 = kXfWarp0 + 4 * NG;
+  static constexpr int kThreads = 32 * (kEpiWarp0 + 4);
+  static_assert(kAlloc <= 232448, "shared memory budget");
+  static_assert(BT <= 32, "decode token tiles");
+  static_assert(kXfWarp0 % 4 == 0, "transform warp q of a group must own TMEM lanes 32q..32q+31");
+};
+
+template <bool BF16, int BT, int RK, int RS, int NG, int SA>
+__global__ void __launch_bounds__(W4TmLayout<BT, RK, RS, NG, SA>::kThreads, 1)
+    w4a16_decode_tm_kernel(const __grid_constant__ CUtensorMap tma_a, const W4Params p) {
+  using L = W4TmLayout<BT, RK, RS, NG, SA>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint64_t* full_raw = reinterpret_cast<uint64_t*>(smem + L::kOffBar);
+  uint64_t* raw_empty = full_raw + RS;
+  uint64_t* slot_full = raw_empty + RS;        // [NG][SA]
+  uint64_t* slot_empty = slot_full + NG * SA;  // [NG][SA]
+  uint64_t* acc_full = slot_empty + NG * SA;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffMisc + 4);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int kEpiWarp0 = L::kEpiWarp0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < RS; ++s) {
+      mbar_init(&full_raw[s], 1);
+      mbar_init(&raw_empty[s], 4 * NG + NG);  // every transform warp + each MMA warp's commit
+    }
+    for (int s = 0; s < NG * SA; ++s) {
+      mbar_init(&slot_full[s], 4);   // the group's transform warps
+      mbar_init(&slot_empty[s], 1);  // the group's MMA commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], NG);  // one commit per MMA warp
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, NG);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch_desc(&tma_a);
+  if (warp == L::kMmaWarp0) {
+    tmem_alloc(tmem_slot, L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- producer (whole warp loops, one elected lane issues)
+    int rs = 0;
+    uint32_t rph = 0, live = 0, live_par = 0;
+    bool ok = true;
+    int64_t cur = w4_first(p);
+    W4Seg s;
+    while (ok && w4_next(p, cur, s)) {
+      for (int kb = s.kb0; kb < s.kb1; kb += RK) {
+        const int n = s.kb1 - kb < RK ? s.kb1 - kb : RK;
+        const int g_lo = (kb * 64) >> p.gshift, g_hi = ((kb + n) * 64 - 1) >> p.gshift;
+        const int ng = g_hi - g_lo + 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, kSiteProducer, p.status));
+        if (!ok) break;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&full_raw[rs], static_cast<uint32_t>(n * (kW4Chunk + L::kAct) + ng * kW4GroupBytes));
+          bulk_load(smem + L::kOffWords + rs * L::kWords,
+                    p.tiles + (static_cast<int64_t>(s.tn) * p.KB + kb) * kW4Chunk, n * kW4Chunk, &full_raw[rs]);
+          bulk_load(smem + L::kOffGrp + rs * L::kGrp,
+                    p.groups + (static_cast<int64_t>(s.tn) * p.G + g_lo) * kW4GroupBytes, ng * kW4GroupBytes,
+                    &full_raw[rs]);
+          for (int j = 0; j < n; ++j)
+            tma_load_2d(&tma_a, &full_raw[rs], smem + L::kOffAct + (rs * RK + j) * L::kAct, (kb + j) * 64, 0);
+        }
+        __syncwarp();
+        live |= 1u << rs;
+        live_par = (live_par & ~(1u << rs)) | (rph << rs);
+        if (++rs == RS) {
+          rs = 0;
+          rph ^= 1u;
+        }
+      }
+    }
+    for (int i = 0; i < RS && ok; ++i) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&raw_empty[rs], rph ^ 1u, abort_flag, kSiteProducer, p.status));
+      if (++rs == RS) {
+        rs = 0;
+        rph ^= 1u;
+      }
+    }
+    if (!ok && lane == 0) {
+      const uint64_t t0 = globaltimer();
+      for (int i = 0; i < RS; ++i)
+        if ((live >> i) & 1u)
+          while (!mbar_try_wait(&full_raw[i], (live_par >> i) & 1u) && globaltimer() - t0 < kWaitLimitNs) {
+          }
+    }
+  } else if (warp < L::kXfWarp0) {
+    // ---- MMA warp of group g: the k-blocks i = g, g + NG, ... of this CTA's
+    // sequence, into the group's own accumulator.  Whole warp loops, one
+    // elected lane (always the same) issues and commits.
+    const int g = warp - L::kMmaWarp0;
+    constexpr uint32_t idesc = (1u << 4) | (BF16 ? (1u << 7) | (1u << 10) : 0u) |
+                               (static_cast<uint32_t>(BT >> 3) << 17) |
+                               (static_cast<uint32_t>(kW4Rows >> 4) << 24);
+    const uint32_t a_tmem0 = tmem_base + L::kSlot0 + static_cast<uint32_t>(g * SA * 32);
+    const uint64_t b_desc0 = sw128_desc(smem_u32(smem + L::kOffAct));
+    int rs = 0, i = 0, jg = 0, seg_i = 0;
+    bool ok = true;
+    int64_t cur = w4_first(p);
+    W4Seg s;
+    while (ok && w4_next(p, cur, s)) {
+      const int b = seg_i & 1;
+      const uint32_t d = tmem_base + static_cast<uint32_t>((b * NG + g) * BT);
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait(&acc_empty[b], ((seg_i >> 1) & 1) ^ 1u, abort_flag, kSiteMmaTmem, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t acc = 0;
+      for (int kb = s.kb0; kb < s.kb1 && ok; kb += RK) {
+        const int n = s.kb1 - kb < RK ? s.kb1 - kb : RK;
+        for (int j = 0; j < n; ++j, ++i) {
+          if (i % NG != g) continue;
+          const int sl = jg % SA;
+          ok = __all_sync(0xffffffffu,
+                          mbar_wait(&slot_full[g * SA + sl], (jg / SA) & 1, abort_flag, kSiteMma, p.status));
+          if (!ok) break;
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t at = a_tmem0 + static_cast<uint32_t>(sl * 32);
+            const uint64_t bd = b_desc0 + static_cast<uint32_t>(((rs * RK + j) * L::kAct) >> 4);
+            umma_ts_f16(d, at, bd, idesc, acc);
+            umma_ts_f16(d, at + 8, bd + 2, idesc, 1u);
+            umma_ts_f16(d, at + 16, bd + 4, idesc, 1u);
+            umma_ts_f16(d, at + 24, bd + 6, idesc, 1u);
+            umma_commit(&slot_empty[g * SA + sl]);
+          }
+          __syncwarp();
+          acc = 1;
+          ++jg;
+        }
+        if (!ok) break;
+        // the stage's activation tiles are free once this warp's MMAs are done
+        if (elect_one()) umma_commit(&raw_empty[rs]);
+        __syncwarp();
+        if (++rs == RS) rs = 0;
+      }
+      if (!ok) break;
+      if (elect_one()) umma_commit(&acc_full[b]);
+      __syncwarp();
+      ++seg_i;
+    }
+    // Before TMEM is released: every MMA of every group complete.
+    if (elect_one()) umma_commit(drain);
+    __syncwarp();
+    if (g == 0 && lane == 0) {
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < kWaitLimitNs) {
+      }
+    }
+    __syncwarp();
+  } else if (warp < kEpiWarp0) {
+    // ---- transform, group g of 4 warps; thread = weight row r = TMEM lane r.
+    // Each warp dequantizes its 32 rows of a k-block into 32 registers per
+    // thread (two 16-bit weights per register, K order) and stores them into
+    // the group's TMEM slot with one tcgen05.st; it arrives on the slot's full
+    // barrier once its stores have completed.
+    const int t = threadIdx.x - 32 * L::kXfWarp0;
+    const int g = t >> 7, r = t & 127;
+    const uint32_t slot_row = tmem_base + (static_cast<uint32_t>(r & ~31) << 16) + L::kSlot0 +
+                              static_cast<uint32_t>(g * SA * 32);
+    int rs = 0, i = 0, jg = 0;
+    uint32_t rph = 0;
+    bool ok = true;
+    int64_t cur = w4_first(p);
+    W4Seg s;
+    while (ok && w4_next(p, cur, s)) {
+      for (int kb = s.kb0; kb < s.kb1; kb += RK) {
+        const int n = s.kb1 - kb < RK ? s.kb1 - kb : RK;
+        const int g_lo = (kb * 64) >> p.gshift;
+        ok = __all_sync(0xffffffffu, mbar_wait(&full_raw[rs], rph, abort_flag, kSiteTransform, p.status));
+        if (!ok) break;
+        const uint32_t words = smem_u32(smem + L::kOffWords + rs * L::kWords) + r * 32;
+        const uint32_t grp = smem_u32(smem + L::kOffGrp + rs * L::kGrp) + r * 4;
+        for (int j = 0; j < n; ++j, ++i) {
+          if (i % NG != g) continue;
+          const int sl = jg % SA;
+          // loads and dequantization first; the slot wait only gates the TMEM store
+          const uint4 wa = lds_v4(words + j * kW4Chunk);
+          const uint4 wb = lds_v4(words + j * kW4Chunk + 16);
+          const int ga = (((kb + j) * 64) >> p.gshift) - g_lo;
+          const int gb = (((kb + j) * 64 + 32) >> p.gshift) - g_lo;
+          uint32_t za, sa, zb, sb;
+          group_operands<BF16>(lds_u32(grp + ga * kW4Rows * 4), za, sa);
+          group_operands<BF16>(lds_u32(grp + gb * kW4Rows * 4), zb, sb);
+          uint32_t v[32];
+          const uint32_t w8[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 d4 = dequant_word<BF16>(w8[q], q < 4 ? za : zb, q < 4 ? sa : sb);
+            v[4 * q] = d4.x;
+            v[4 * q + 1] = d4.y;
+            v[4 * q + 2] = d4.z;
+            v[4 * q + 3] = d4.w;
+          }
+          ok = __all_sync(0xffffffffu, mbar_wait(&slot_empty[g * SA + sl], ((jg / SA) & 1) ^ 1u, abort_flag,
+                                                 kSiteTransform, p.status));
+          if (!ok) break;
+          tc_fence_after();  // the slot's previous MMAs have read it
+          tmem_st32(slot_row + static_cast<uint32_t>(sl * 32), v);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&slot_full[g * SA + sl]);
+          ++jg;
+        }
+        if (!ok) break;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[rs]);  // this warp's reads of the stage are over
+        if (++rs == RS) {
+          rs = 0;
+          rph ^= 1u;
+        }
+      }
+    }
+  } else {
+    // ---- epilogue: TMEM lane = weight row, column = token; sums the NG
+    // group accumulators of a segment in group order.  A row tile split
+    // across CTAs c_lo..c_hi is finished by c_lo, which covers the tile's
+    // first k-blocks at the end of its range; the other CTAs cover it at the
+    // start of theirs, publish fp32 slots and bump the tile's arrival
+    // counter.  c_lo keeps its own sums in registers, waits (bounded) for the
+    // count, adds the slots in CTA order, writes the output and resets the
+    // counter to zero for the next call.  Waits only ever point at CTAs of
+    // higher index, which finish their part first.
+    const int quarter = warp & 3;
+    const int rt = quarter * 32 + lane;
+    const int e0 = 32 * kEpiWarp0;
+    const int me = static_cast<int>(blockIdx.x);
+    int seg_i = 0, i0 = 0;
+    bool ok = true;
+    int64_t cur = w4_first(p);
+    W4Seg s;
+    while (ok && w4_next(p, cur, s)) {
+      const int b = seg_i & 1;
+      const int len = s.kb1 - s.kb0;
+      ok = bar_and(1, 128, mbar_wait(&acc_full[b], (seg_i >> 1) & 1, abort_flag, kSiteEpilogue, p.status));
+      if (!ok) break;
+      tc_fence_after();
+      const int n = s.tn * kW4Rows + rt;
+      const int mc = p.M < BT ? p.M : BT;
+      const int64_t u0 = static_cast<int64_t>(s.tn) * p.KB;
+      const int c_lo = w4_owner(p.U, p.P, u0), c_hi = w4_owner(p.U, p.P, u0 + p.KB - 1);
+      const bool finisher = me == c_lo;
+      float y[BT];
+#pragma unroll
+      for (int j = 0; j < BT; ++j) y[j] = 0.0f;
+#pragma unroll
+      for (int c0 = 0; c0 < BT; c0 += 16) {
+        if (c0 < mc) {
+#pragma unroll
+          for (int gg = 0; gg < NG; ++gg) {
+            // group gg holds k-blocks of this segment iff one is = gg mod NG
+            if (len >= NG || (((gg - i0) % NG + NG) % NG) < len) {
+              uint32_t v[16];
+              tmem_ld16(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                            static_cast<uint32_t>((b * NG + gg) * BT + c0),
+                        v);
+              tmem_ld_wait16(v);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) y[c0 + j] = __fadd_rn(y[c0 + j], __uint_as_float(v[j]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);  // TMEM buffer free for the groups
+      if (!finisher) {
+        // Publish this CTA's share of the tile (token columns past M are 0).
+        float* prow = p.partial + (static_cast<int64_t>(s.slot) * kW4Rows + rt) * BT;
+#pragma unroll
+        for (int q = 0; q < BT / 4; ++q)
+          *reinterpret_cast<float4*>(prow + 4 * q) = make_float4(y[4 * q], y[4 * q + 1], y[4 * q + 2], y[4 * q + 3]);
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (static_cast<int>(threadIdx.x) == e0) atomicAdd(&p.counters[c_lo], 1);
+      } else {
+        if (c_hi > c_lo) {
+          bool arrived = true;
+          if (static_cast<int>(threadIdx.x) == e0)
+            arrived = wait_count(&p.counters[me], c_hi - c_lo, abort_flag, p.status);
+          ok = bar_and(1, 128, arrived);
+          if (!ok) break;
+          __threadfence();
+          for (int c = c_lo + 1; c <= c_hi; ++c) {
+            const float4* src =
+                reinterpret_cast<const float4*>(p.partial + (static_cast<int64_t>(s.tn + c) * kW4Rows + rt) * BT);
+#pragma unroll
+            for (int q = 0; q < BT / 4; ++q) {
+              const float4 v = __ldcg(src + q);
+              y[4 * q] = __fadd_rn(y[4 * q], v.x);
+              y[4 * q + 1] = __fadd_rn(y[4 * q + 1], v.y);
+              y[4 * q + 2] = __fadd_rn(y[4 * q + 2], v.z);
+              y[4 * q + 3] = __fadd_rn(y[4 * q + 3], v.w);
+            }
+          }
+          if (static_cast<int>(threadIdx.x) == e0) p.counters[me] = 0;
+        }
+        if (n < p.N) {
+          const float bias = p.bias != nullptr ? load_as_float(p.bias, p.bias_dtype, n) : 0.0f;
+#pragma unroll
+          for (int j = 0; j < BT; ++j) {
+            if (j < mc) {
+              const float o32 = __fadd_rn(y[j], bias);
+              uint16_t* o = static_cast<uint16_t*>(p.out) + static_cast<int64_t>(j) * p.ldo + n;
+              *o = BF16 ? __bfloat16_as_ushort(__float2bfloat16_rn(o32)) : __half_as_ushort(__float2half_rn(o32));
+            }
+          }
+        }
+      }
+      i0 += len;
+      ++seg_i;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == L::kMmaWarp0) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::kTmemCols);
+  }
+}
+
 // PackedInt4 words (signed nibbles q = u - 8; layout "nk" [N, K/8] or "kn"
 // [K/8, N]; element j at nibble j, or 7 - j for order "high") -> W4A16 tiles.
 // One thread per output word; rows past N become 0.
@@ -1052,6 +1409,31 @@ static cudaError_t launch_w4_decode(const void* a, int64_t lda, const W4Params& 
   return cudaGetLastError();
 }
 
+template <bool BF16, int BT, int RK, int RS, int NG, int SA>
+static cudaError_t launch_w4_decode_tm(const void* a, int64_t lda, const W4Params& p, cudaStream_t stream) {
+  using L = W4TmLayout<BT, RK, RS, NG, SA>;
+  auto kernel = w4a16_decode_tm_kernel<BF16, BT, RK, RS, NG, SA>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return e;
+    configured[dev] = true;
+  }
+  CUtensorMap ma;
+  cudaError_t e = act_map(&ma, a, p.K, p.M, lda, BT);
+  if (e != cudaSuccess) return e;
+  kernel<<<p.P, L::kThreads, L::kAlloc, stream>>>(ma, p);
+  return cudaGetLastError();
+}
+
+// Decode-kernel selection (M <= 32): 0 = automatic (TMEM operands), 1 = the
+// shared-memory-operand kernel, 2 = the TMEM-operand kernel.
+static int g_w4_decode_path = 0;
+void set_w4a16_path(int path) { g_w4_decode_path = path; }
+
 // Token tile for M tokens; M <= 32 runs stream-K over one token tile.
 static int w4_bt(int64_t M) { return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256; }
 
@@ -1115,9 +1497,18 @@ cudaError_t run_w4a16(const void* a, int a_dtype, int64_t lda, const void* tiles
   const bool bf = a_dtype == kBF16;
   cudaError_t e;
   if (pl.streamk) {
+    if (g_w4_decode_path == 1) {
+      if (pl.bt == 16)
+        return bf ? launch_w4_decode<true, 16, 4, 4, 3>(a, lda, p, stream) : launch_w4_decode<false, 16, 4, 4, 3>(a, lda, p, stream);
+      return bf ? launch_w4_decode<true, 32, 4, 3, 3>(a, lda, p, stream) : launch_w4_decode<false, 32, 4, 3, 3>(a, lda, p, stream);
+    }
+    // dequantized k-blocks in TMEM: 4 slots per group at 16 tokens, 3 at 32,
+    // and the shared memory they no longer need deepens the raw ring
     if (pl.bt == 16)
-      return bf ? launch_w4_decode<true, 16, 4, 4, 3>(a, lda, p, stream) : launch_w4_decode<false, 16, 4, 4, 3>(a, lda, p, stream);
-    return bf ? launch_w4_decode<true, 32, 4, 3, 3>(a, lda, p, stream) : launch_w4_decode<false, 32, 4, 3, 3>(a, lda, p, stream);
+      return bf ? launch_w4_decode_tm<true, 16, 4, 7, 3, 4>(a, lda, p, stream)
+                : launch_w4_decode_tm<false, 16, 4, 7, 3, 4>(a, lda, p, stream);
+    return bf ? launch_w4_decode_tm<true, 32, 4, 6, 3, 3>(a, lda, p, stream)
+              : launch_w4_decode_tm<false, 32, 4, 6, 3, 3>(a, lda, p, stream);
   }
   switch (pl.bt) {
 #define W4_CASE(BT, RK, RS, XS, UK)                                                                     \

@@ -239,6 +239,16 @@ def quantize_w4a16(w, *, group_size=128, dtype=torch.bfloat16):
     return prepare_w4a16(pack_int4(w, group_size=group_size, symmetric=False), dtype)
 
 
+def set_w4a16_path(path):
+    """Process-wide W4A16 decode kernel for M <= 32: "auto", "smem" (the
+    dequantized weights staged in shared memory) or "tmem" (kept in tensor
+    memory as the MMA's A operand).  Both dequantize identically; outputs
+    differ only in the tensor core's fp32 summation order.  A tuning and
+    verification knob."""
+    code = {"auto": 0, "smem": 1, "tmem": 2}[path]
+    nat.check(nat.library().b2_set_w4a16_path(code), "b2_set_w4a16_path")
+
+
 def w4a16_gemm(a, wt, bias=None, *, workspace=None):
     """y = a @ dequant(wt).T (+ bias) on the tcgen05 W4A16 kernel."""
     if not isinstance(wt, W4A16Weight):

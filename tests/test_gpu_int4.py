@@ -132,10 +132,17 @@ def test_w4a16_small_shapes(dtype, m, n, k, g):
     _check(y, ref, absref, dtype, bias)
 
 
+@pytest.fixture(params=["tmem", "smem"])
+def w4_path(request):
+    i4.set_w4a16_path(request.param)
+    yield request.param
+    i4.set_w4a16_path("auto")
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("m", [1, 2, 3, 5, 16, 17, 40, 64, 100, 128, 129, 300])
 @pytest.mark.parametrize("g", [32, 128])
-def test_w4a16_schedules(dtype, m, g):
+def test_w4a16_schedules(dtype, m, g, w4_path):
     """Stream-K (M <= 128: a CTA's range crosses tiles, group stages start
     mid-group) and whole-tile (M > 128, ragged token and row tiles) runs
     against the oracle; N = 1000 leaves a partial last row tile."""
@@ -166,7 +173,7 @@ def config3_pack():
 
 
 @pytest.mark.parametrize("m", [1, 16, 128, 2048])
-def test_w4a16_config3(m, config3_pack):
+def test_w4a16_config3(m, config3_pack, w4_path):
     """bf16 A [M,4096] ~ N(0,1) against the CPU-packed
     weight, bf16 out; every one of the M x 14336 outputs checked."""
     dtype = torch.bfloat16
@@ -178,7 +185,7 @@ def test_w4a16_config3(m, config3_pack):
     _check(y, ref, absref, dtype, what=f"config3 M={m}")
 
 
-def test_w4a16_deterministic_split_k():
+def test_w4a16_deterministic_split_k(w4_path):
     dtype = torch.bfloat16
     gen = torch.Generator(device="cuda").manual_seed(3)
     w = torch.randn((4096, 4096), generator=gen, device="cuda") * 0.02
