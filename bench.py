@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--sets", type=int, default=4, help="input sets cycled to defeat L2 reuse")
+    ap.add_argument("--column-parallel", action="store_true",
+                    help="c5 on one GPU through the column-parallel stack (the N > 1 code path, eager calls)")
     ap.add_argument("--workload", default="c2",
                     help="c2 (headline, default), c1, c3m1/c3m16/c3m128/c3m2048 (W4A16), "
                          "c4m1/c4m2048 (FP8), w4a8m<M> (W4A8), c5 (28-block W8A8 DiT stack; also "
@@ -773,7 +775,8 @@ def run_c5_multi(args, rank, world, local_rank):
     torch.cuda.empty_cache()
 
     def barrier():
-        dist.barrier(device_ids=[local_rank])
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
 
     for _ in range(max(3, args.warmup)):
         y = stack(x0)
@@ -791,7 +794,9 @@ def run_c5_multi(args, rank, world, local_rank):
         e1.record(stream)
         torch.cuda.synchronize()
     barrier()
-    ms = _max_over_ranks(torch, dist, dev, e0.elapsed_time(e1) / steps)
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        ms = _max_over_ranks(torch, dist, dev, ms)
     status = nat.device_status()
     g.close()
     if rank != 0:
@@ -1260,7 +1265,7 @@ def main():
         if rank == 0:
             run_moss(args)
         return
-    if args.workload not in ("c2", "c5") or (args.workload == "c5" and world == 1):
+    if args.workload not in ("c2", "c5") or (args.workload == "c5" and world == 1 and not args.column_parallel):
         if rank == 0:
             run_workload(args)
         return
@@ -1272,7 +1277,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        if world > 1 and args.workload == "c5":
+        if args.workload == "c5":
             run_c5_multi(args, rank, world, local_rank)
         elif world > 1:
             run_b200_multi(args, rank, world, local_rank)

@@ -77,11 +77,13 @@ class PeerGather:
         self.epoch = 0
         self._imported = []
         mine = [self._export(t) for t in self.local + [self.state]]
-        if exchange is None:
+        if exchange is not None:
+            everyone = exchange(mine)
+        elif self.world == 1:
+            everyone = [mine]
+        else:
             everyone = [None] * self.world
             dist.all_gather_object(everyone, mine, group=group)
-        else:
-            everyone = exchange(mine)
         ptrs = [[None] * self.world for _ in range(buffers + 1)]
         for r, entries in enumerate(everyone):
             for i, (handle, offset) in enumerate(entries):
