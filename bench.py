@@ -179,6 +179,23 @@ def torch_cpu_baseline(budget_s, threads):
                       f"{threads} torch threads"}
 
 
+def c2_config(world, sets):
+    """The config dict of the config-2 line at `world` GPUs (both arms print it)."""
+    if world == 1:
+        return {"workload": "config2: W8A8 INT8 linear with block-128 Hadamard rotation, "
+                            "fp16 X[4096,3072] (1% outlier channels x20) -> fp16 Y[4096,12288]",
+                "M": M, "N": N, "N_per_rank": N, "K": K, "rotation_block": ROT, "parallelism": "single GPU",
+                "l2": f"inputs cycled over {sets} buffer sets "
+                      f"({sets * (M * K * 2 + N * K) / 2**20:.0f} MiB > 126 MB L2)"}
+    return {"workload": "config2 column-parallel: W8A8 INT8 linear with block-128 Hadamard rotation, "
+                        "fp16 X[4096,3072] -> fp16 Y[4096,12288], N sharded over the ranks, Y reassembled "
+                        "on every rank inside the step",
+            "M": M, "N": N, "N_per_rank": N // world, "K": K, "rotation_block": ROT,
+            "parallelism": f"column-parallel N-shard x{world}, output gather fused into the GEMM epilogue "
+                           "(NVLink peer stores)",
+            "l2": f"inputs cycled over {sets} buffer sets, output buffers alternate (> 126 MB L2)"}
+
+
 def run_reference(args, rank):
     """--impl reference: the CPU oracle port on the host cores (rank 0 only)."""
     if rank != 0:
@@ -205,15 +222,17 @@ def run_reference(args, rank):
         step()
     dt = (time.perf_counter() - t0) / max(1, args.steps)
     value = 2.0 * rows * N * K / dt / 1e12
+    torch_leg = torch_cpu_baseline(min(10.0, args.cpu_budget_s), threads)
     line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "config2 W8A8 rotated linear, CPU sample",
-                       "M": M, "N": N, "K": K, "rotation_block": ROT, "sample_rows": rows},
+            "config": c2_config(args.gpus, args.sets),
+            "torch_reference_math": torch_leg,
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
                              "kind": "port",
-                             "sample": f"{rows} of {M} tokens per step (oracle port, C/OpenMP)"},
+                             "sample": f"{rows} of {M} tokens per step, the whole {N}-column layer on the host "
+                                       f"(oracle port, C/OpenMP)"},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -477,12 +496,7 @@ def run_b200(args, rank, world, local_rank):
         "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic",
-        "config": {"workload": "config2: W8A8 INT8 linear with block-128 Hadamard rotation, "
-                               "fp16 X[4096,3072] (1% outlier channels x20) -> fp16 Y[4096,12288]",
-                   "M": M, "N": N, "N_per_rank": N, "K": K, "rotation_block": ROT,
-                   "parallelism": "single GPU",
-                   "l2": f"inputs cycled over {args.sets} buffer sets "
-                         f"({args.sets * (M * K * 2 + N * K) / 2**20:.0f} MiB > 126 MB L2)"},
+        "config": c2_config(1, args.sets),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
                      "unit": "TOPS", "frac": round(achieved / int8_peak, 4), "traffic": None,
                      "traffic_note": "not measured in this run (no profiler inside the bench); the ncu capture "
@@ -700,13 +714,7 @@ def run_b200_multi(args, rank, world, local_rank):
         "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic",
-        "config": {"workload": "config2 column-parallel: W8A8 INT8 linear with block-128 Hadamard rotation, "
-                               "fp16 X[4096,3072] -> fp16 Y[4096,12288], N sharded over the ranks, Y reassembled "
-                               "on every rank inside the step",
-                   "M": M, "N": N, "N_per_rank": ns, "K": K, "rotation_block": ROT,
-                   "parallelism": f"column-parallel N-shard x{world}, output gather fused into the GEMM epilogue "
-                                  "(NVLink peer stores)",
-                   "l2": f"inputs cycled over {args.sets} buffer sets, output buffers alternate (> 126 MB L2)"},
+        "config": c2_config(world, args.sets),
         "roofline": {"bound": "nvlink" if t_link >= t_gemm else "tensor", "achieved_ms": round(ms, 5),
                      "target_ms": round(target, 5), "frac": round(target / ms, 4),
                      "nvlink_bytes_received_per_rank": recv, "nvlink_gbs_ref": nvlink_gbs,
