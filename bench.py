@@ -53,6 +53,7 @@ def parse():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--cpu-budget-s", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sustained", action="store_true", help="skip the >= 1 s sustained leg (profiling runs)")
     ap.add_argument("--sets", type=int, default=4, help="input sets cycled to defeat L2 reuse")
     ap.add_argument("--column-parallel", action="store_true",
                     help="c5 on one GPU through the column-parallel stack (the N > 1 code path, eager calls)")
@@ -418,7 +419,7 @@ def run_b200(args, rank, world, local_rank):
     value = 2.0 * M * N * K / (ms * 1e-3) / 1e12
 
     # ---- sustained: the same step back to back for >= 1 s (clock record beside it)
-    n_sus = max(args.steps, int(1.0 / (ms * 1e-3)) + 1)
+    n_sus = args.steps if args.no_sustained else max(args.steps, int(1.0 / (ms * 1e-3)) + 1)
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as sus_clocks:
         e0.record(stream)

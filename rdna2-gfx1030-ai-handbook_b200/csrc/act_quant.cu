@@ -357,7 +357,7 @@ __device__ __forceinline__ uint32_t code_markstein(float v, float s, float r) {
   return __float_as_uint(__fadd_rn(z, 12582912.0f));  // low byte = rint(z), |z| <= 127
 }
 
-template <int DT, int E = kLaneE>
+template <int DT, bool FP8 = false, int E = kLaneE>
 __global__ void __launch_bounds__(kLaneThreads, 1)
     act_quant_lane_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int tpr, int rows_per_cta,
                           int block, float inv, uint8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale,
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
     __syncthreads();
     if (!live) continue;
     amax = __uint_as_float(s_max[sb][r_local]);
-    float sc = __fdiv_rn(amax, 127.0f);
+    float sc = __fdiv_rn(amax, FP8 ? 448.0f : 127.0f);
     if (!(sc > 0.0f)) sc = 1.0f;
 
     uint8_t* dst = q + row * ldq + static_cast<int64_t>(part) * E;
@@ -488,25 +488,42 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
       const float r = __frcp_rn(s2);
       const float2 r2 = make_float2(r, r), ns2 = make_float2(-s2, -s2);
       const float2 magic = make_float2(12582912.0f, 12582912.0f);
-      // codes of the pair i (Markstein, as code_markstein): y = v*r,
-      // e = v - s*y exactly, RN(v/s) = y + e*r, + 1.5*2^23 -> low byte
-      auto codes = [&](int i, uint32_t& lo, uint32_t& hi) {
+      // the exact quotient of the pair i (Markstein, as code_markstein):
+      // y = v*r, e = v - s*y exactly, RN(v/s) = y + e*r
+      auto quotient = [&](int i) {
         const float2 y = __fmul2_rn(w[i], r2);
         const float2 e = __ffma2_rn(ns2, y, w[i]);
-        const float2 z = __ffma2_rn(e, r2, y);
-        const float2 m = __fadd2_rn(z, magic);
+        return __ffma2_rn(e, r2, y);
+      };
+      // int8: + 1.5*2^23 leaves the ties-to-even integer in the low byte
+      auto codes = [&](int i, uint32_t& lo, uint32_t& hi) {
+        const float2 m = __fadd2_rn(quotient(i), magic);
         lo = __float_as_uint(m.x);
         hi = __float_as_uint(m.y);
+      };
+      // e4m3: one round-to-nearest-even, saturating conversion of the pair
+      // (e4m3_rn_sat(RN(v/s)), the oracle's b2o_f32_to_e4m3).  The quotient
+      // takes v's sign: RN(v/s) has it for every v (s > 0), but the FMA
+      // correction turns a -0 input into +0, and e4m3 keeps the sign of zero.
+      auto codes_e4m3 = [&](int i) {
+        float2 z = quotient(i);
+        z.x = copysignf(z.x, w[i].x);
+        z.y = copysignf(z.y, w[i].y);
+        return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(z, __NV_SATFINITE, __NV_E4M3));
       };
 #pragma unroll
       for (int j = 0; j < E / 16; ++j) {
         uint32_t o[4];
 #pragma unroll
         for (int t2 = 0; t2 < 4; ++t2) {
-          uint32_t c0, c1, c2, c3;
-          codes(8 * j + 2 * t2, c0, c1);
-          codes(8 * j + 2 * t2 + 1, c2, c3);
-          o[t2] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+          if constexpr (FP8) {
+            o[t2] = codes_e4m3(8 * j + 2 * t2) | (codes_e4m3(8 * j + 2 * t2 + 1) << 16);
+          } else {
+            uint32_t c0, c1, c2, c3;
+            codes(8 * j + 2 * t2, c0, c1);
+            codes(8 * j + 2 * t2 + 1, c2, c3);
+            o[t2] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
+          }
         }
         *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(o[0], o[1], o[2], o[3]);
       }
@@ -517,8 +534,13 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
 #pragma unroll
         for (int t2 = 0; t2 < 4; ++t2) {
           const float2 p0 = w[8 * j + 2 * t2], p1 = w[8 * j + 2 * t2 + 1];
-          o[t2] = __byte_perm(__byte_perm(slow_int8(p0.x, sc), slow_int8(p0.y, sc), 0x0040),
-                              __byte_perm(slow_int8(p1.x, sc), slow_int8(p1.y, sc), 0x0040), 0x5410);
+          if constexpr (FP8) {
+            o[t2] = quant_e4m3(p0.x, sc, 0.0f, false) | (quant_e4m3(p0.y, sc, 0.0f, false) << 8) |
+                    (quant_e4m3(p1.x, sc, 0.0f, false) << 16) | (quant_e4m3(p1.y, sc, 0.0f, false) << 24);
+          } else {
+            o[t2] = __byte_perm(__byte_perm(slow_int8(p0.x, sc), slow_int8(p0.y, sc), 0x0040),
+                                __byte_perm(slow_int8(p1.x, sc), slow_int8(p1.y, sc), 0x0040), 0x5410);
+          }
         }
         *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(o[0], o[1], o[2], o[3]);
       }
@@ -536,10 +558,10 @@ void set_prologue_path(int path) { g_prologue_path = path; }
 // Small CTAs (about 128 threads: whole rows of TPR lanes), several per SM,
 // so that one CTA's loads overlap another's arithmetic across the per-row
 // barrier.
-template <int DT>
+template <int DT, bool FP8>
 static cudaError_t launch_lane(int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K, int block,
                                float inv, uint8_t* q, int64_t ldq, float* scale, int early) {
-  auto kernel = act_quant_lane_kernel<DT>;
+  auto kernel = act_quant_lane_kernel<DT, FP8>;
   const int tpr = K / kLaneE;
   int rows = 128 / tpr;
   if (rows < 1) rows = 1;
@@ -567,7 +589,7 @@ static cudaError_t launch_lane(int64_t M, cudaStream_t st, const void* x, int64_
 // kLaneThreads), with 16-byte aligned input and code rows and rotation
 // blocks of at most 32 lanes.
 static bool lane_ok(int x_dtype, int quant, int64_t K, int block, bool vin16, bool vout16) {
-  if (quant != 0 || !(x_dtype == kF16 || x_dtype == kBF16 || x_dtype == kF32)) return false;
+  if (quant > 1 || !(x_dtype == kF16 || x_dtype == kBF16 || x_dtype == kF32)) return false;
   if (!vin16 || !vout16 || K % kLaneE != 0 || K / kLaneE > kLaneThreads) return false;
   return block <= 1 || block <= 32 * kLaneE;
 }
@@ -640,10 +662,17 @@ cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int6
     if (g_prologue_path != 1 && lane_ok(x_dtype, quant, K, block, vin16, vout16)) {
       uint8_t* qb = static_cast<uint8_t*>(q);
       const int k = static_cast<int>(K);
+      if (quant == 1) {
+        switch (x_dtype) {
+          case kF32: return launch_lane<kF32, true>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
+          case kF16: return launch_lane<kF16, true>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
+          default: return launch_lane<kBF16, true>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
+        }
+      }
       switch (x_dtype) {
-        case kF32: return launch_lane<kF32>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
-        case kF16: return launch_lane<kF16>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
-        default: return launch_lane<kBF16>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
+        case kF32: return launch_lane<kF32, false>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
+        case kF16: return launch_lane<kF16, false>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
+        default: return launch_lane<kBF16, false>(M, stream, x, ldx, k, block, inv_b, qb, ldq, scale, early);
       }
     }
   }

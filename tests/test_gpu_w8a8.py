@@ -250,12 +250,40 @@ def test_act_quant_extreme_scales(dtype, block, prologue_path):
     assert np.array_equal(q.cpu().numpy(), ref_q)
 
 
-def test_act_quant_e4m3_bit_exact():
-    rng = np.random.default_rng(5)
-    x32 = outlier_activations(rng, 33, 5120)
-    xt = x_tensor(x32, torch.bfloat16)
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("k,block", [(5120, None), (3072, 128), (4096, 1024), (384, 128), (80, 16)])
+def test_act_quant_e4m3_bit_exact(dtype, k, block, prologue_path):
+    """Per-token e4m3 codes (scale absmax/448, e4m3_rn_sat(RN(v/s))) on both
+    prologue kernels, with and without rotation, against the oracle."""
+    rng = np.random.default_rng(5 + k)
+    x32 = outlier_activations(rng, 33, k)
+    x32[2] = 0.0
+    xt = x_tensor(x32, dtype)
+    q, s = rdna2_ops.act_quant(xt, rotation_block=block, quant="e4m3")
+    ref_q, ref_s = oracle.quant_rows_e4m3(oracle.rotate_rows(x_bits(xt), ODT[dtype], block or 0))
+    assert np.array_equal(s.cpu().numpy().view(np.uint32), ref_s.view(np.uint32))
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), ref_q)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_act_quant_e4m3_extreme_scales_and_grid_ties(dtype, prologue_path):
+    """e4m3 codes for scales below 2^-60, above 2^60 and subnormal, and for
+    rows whose quotients fall exactly between two e4m3 values (scale 1:
+    absmax 448) or at the saturation edge."""
+    rng = np.random.default_rng(12)
+    x32 = outlier_activations(rng, 8, 3072)
+    x32[0] *= 1e-25
+    x32[1] *= 1e-39
+    x32[2] *= 1e30
+    x32[3] *= 1e-44 if dtype == torch.float32 else 1e-40
+    x32[4] = 0.0
+    x32[4, 0] = 448.0
+    grid_ties = np.array([1.0625, 1.1875, 17.0, 19.0, 240.0, 272.0, 432.0, 440.0, 0.0068359375], np.float32)
+    x32[4, 1:1 + grid_ties.size] = grid_ties
+    x32[5] = -x32[4]
+    xt = x_tensor(x32, dtype)
     q, s = rdna2_ops.act_quant(xt, quant="e4m3")
-    ref_q, ref_s = oracle.quant_rows_e4m3(oracle.rotate_rows(x_bits(xt), oracle.BF16, 0))
+    ref_q, ref_s = oracle.quant_rows_e4m3(oracle.rotate_rows(x_bits(xt), ODT[dtype], 0))
     assert np.array_equal(s.cpu().numpy().view(np.uint32), ref_s.view(np.uint32))
     assert np.array_equal(q.view(torch.uint8).cpu().numpy(), ref_q)
 
