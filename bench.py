@@ -1083,7 +1083,9 @@ def run_workload(args):
         metric, flops = f"W4A16 GEMM TFLOPS (config 3, M={m})", 2.0 * m * n * k
         launches = 2 if need else 1
         traffic = n * k // 2 + 2 * n * (k // 128) * 2 + m * k * 2 + m * n * 2
-        if m <= 128:
+        # the bound follows the arithmetic intensity against the bf16 ridge
+        # (peak FLOP/s over HBM bytes/s): M = 128 is ~480 FLOP/B, tensor-bound
+        if flops / traffic < pk["bf16_tflops"] * 1e12 / (pk["hbm_gbs"] * 1e9):
             bound, peak, unit = "hbm", pk["hbm_gbs"], "GB/s"
         else:
             bound, peak, unit = "tensor", pk["bf16_tflops"], "TFLOP/s"
@@ -1116,7 +1118,7 @@ def run_workload(args):
         metric, flops = f"W4A8 GEMM TOPS (config-3 shape, M={m})", 2.0 * m * n * k
         launches = 2
         traffic = n * k // 2 + n * (k // 128) * 8 + m * k + m * n * 4
-        if m <= 128:
+        if flops / traffic < 2.0 * pk["bf16_tflops"] * 1e12 / (pk["hbm_gbs"] * 1e9):
             bound, peak, unit = "hbm", pk["hbm_gbs"], "GB/s"
         else:
             bound, peak, unit = "tensor", 2.0 * pk["bf16_tflops"], "TOPS"
