@@ -569,7 +569,20 @@ def run_b200_multi(args, rank, world, local_rank):
     wqs = [wq] + [wq.clone() for _ in range(args.sets - 1)]
     ws_bytes = lib.b2_quant_linear_workspace_bytes(M, K)
     ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
-    g = PeerGather(M * N * world, torch.float16)   # also holds the weak-scaling output (N * world columns)
+    # Every rank maps every peer's buffers; if that fails anywhere, all ranks
+    # agree (one all-reduce) and time the NCCL-gather step instead, saying so.
+    g, peer_error = None, ""
+    try:
+        g = PeerGather(M * N * world, torch.float16)   # also holds the weak-scaling output (N * world columns)
+    except Exception as exc:                           # reported in the line, not swallowed
+        peer_error = f"{type(exc).__name__}: {exc}"[:200]
+    ok_t = torch.tensor([0.0 if g is None else 1.0], device=dev)
+    dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
+    if ok_t.item() < 1.0:
+        if g is not None:
+            g.close()
+        return run_b200_multi_nccl(args, rank, world, local_rank, xs, wq_full, sw_full, bias_full,
+                                   peer_error or "a peer rank could not map the gather buffers")
 
     def gather_step(i, w_rows, sw_rows, b_rows, n_total, col0):
         s = i % args.sets
@@ -749,6 +762,74 @@ def run_b200_multi(args, rank, world, local_rank):
             "fused_gather_gbs_per_rank": round(recv / (ms * 1e-3) / 1e9, 1),
         },
     }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200_multi_nccl(args, rank, world, local_rank, xs, wq_full, sw_full, bias_full, why):
+    """N > 1 when the fused peer gather is unavailable: the rank-local fused
+    linear followed by one NCCL all-gather of the shard outputs inside every
+    step (strong scaling), checked against the 1-GPU linear first."""
+    import torch
+    import torch.distributed as dist
+    import rdna2_ops
+    from rdna2_ops import _native as nat
+
+    dev = torch.device("cuda", local_rank)
+    lib = nat.library()
+    stream = torch.cuda.current_stream(dev)
+    ns = N // world
+    c0 = rank * ns
+    wq = wq_full[c0:c0 + ns].contiguous()
+    sw = sw_full[c0:c0 + ns].contiguous()
+    bias = bias_full[c0:c0 + ns].contiguous()
+    wqs = [wq] + [wq.clone() for _ in range(args.sets - 1)]
+    ws_bytes = lib.b2_quant_linear_workspace_bytes(M, K)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    out_local = torch.empty((M, ns), device=dev, dtype=torch.float16)
+    gathered = torch.empty((world * M, ns), device=dev, dtype=torch.float16)
+
+    def step(i):
+        s = i % args.sets
+        nat.check(lib.b2_quant_linear(nat.KIND_I8, xs[s].data_ptr(), nat.F16, M, K, K, ROT, wqs[s].data_ptr(), K, ns,
+                                      sw.data_ptr(), ns, bias.data_ptr(), nat.F16, nat.EPI_SEPARATE,
+                                      out_local.data_ptr(), nat.F16, ns, ws.data_ptr(), ws_bytes, stream.cuda_stream),
+                  "b2_quant_linear")
+        dist.all_gather_into_tensor(gathered, out_local)
+
+    step(0)
+    torch.cuda.synchronize()
+    ref = rdna2_ops.w8a8_linear(xs[0], wq_full, sw_full, bias_full, rotation_block=ROT, out_dtype=torch.float16)
+    full = gathered.view(world, M, ns).permute(1, 0, 2).reshape(M, N)
+    assert torch.equal(full.view(torch.int16), ref.view(torch.int16)), "gathered output differs from 1-GPU linear"
+    del ref, full
+    for i in range(max(3, args.warmup)):
+        step(i)
+    dist.barrier(device_ids=[local_rank])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier(device_ids=[local_rank])
+    ms = _max_over_ranks(torch, dist, dev, e0.elapsed_time(e1) / args.steps)
+    status = nat.device_status()
+    if rank != 0:
+        return
+    recv = (world - 1) * M * ns * 2
+    cfg = c2_config(world, args.sets)
+    cfg["parallelism"] = f"column-parallel N-shard x{world}, NCCL all-gather of the shard outputs ([P, M, N/P])"
+    line = {"metric": METRIC, "value": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 2), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": cfg,
+            "roofline": {"bound": "nvlink", "achieved_ms": round(ms, 5),
+                         "link_floor_ms": round(recv / 770e9 * 1e3, 5),
+                         "frac": round(recv / 770e9 * 1e3 / ms, 4)},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
+            "device_status": status, "fused_gather_unavailable": why}
     print(json.dumps(line), flush=True)
 
 
