@@ -580,7 +580,8 @@ def run_b200_multi(args, rank, world, local_rank):
     dist.all_reduce(ok_t, op=dist.ReduceOp.MIN)
     if ok_t.item() < 1.0:
         if g is not None:
-            g.close()
+            g.close(barrier=False)
+        dist.barrier(device_ids=[local_rank])          # every rank, mapped or not
         return run_b200_multi_nccl(args, rank, world, local_rank, xs, wq_full, sw_full, bias_full,
                                    peer_error or "a peer rank could not map the gather buffers")
 

@@ -106,11 +106,16 @@ class PeerGather:
         self._imported.append(handle)
         return ptr.value
 
-    def close(self):
-        """Unmap the peers' buffers (every rank's calls must have completed)."""
+    def close(self, barrier=True):
+        """Unmap the peers' buffers.  Collective by default: every rank calls
+        it after its last gathered call, and it returns only when every rank
+        has unmapped, so no rank frees buffers a peer still maps (a caller
+        that synchronizes the ranks itself passes barrier=False)."""
         torch.cuda.synchronize(self.device)
         while self._imported:
             nat.check(self.lib.b2_ipc_release(self._imported.pop()), "b2_ipc_release")
+        if barrier and self.world > 1 and dist.is_initialized():
+            dist.barrier(group=self.group)
 
     def next_slot(self):
         """(epoch, buffer index) of the next call."""
