@@ -182,34 +182,42 @@ def _kitchen_parts():
     return eager_backend, eager, registry
 
 
+def module_api(binding):
+    """The reference module's public functions (comfy_int8.py:71-227,
+    production/MOSS_RDNA2_INT8/backend.py:71-204) bound to one
+    KitchenInt8Binding: (int8_linear, install_backend, disable_backend,
+    get_stats, reset_stats, kitchen_int8_without_transpose_copy).  Each module
+    that exposes the API owns its binding, so installation state and
+    statistics stay separate per module as in the reference."""
+
+    def int8_linear(x, weight, weight_scale, bias=None, out_dtype=torch.bfloat16, convrot=False,
+                    convrot_groupsize=256, input_act=None, input_act_weight=None, input_act_eps=0.0,
+                    residual=None, residual_scale=None):
+        """Kitchen's eager INT8 linear semantics on the B200 kernels: input
+        activation, ConvRot, per-token INT8, GEMM, (acc*(sx*sw)).to(out) + bias,
+        residual."""
+        return binding.int8_linear(x, weight, weight_scale, bias, out_dtype, convrot, convrot_groupsize,
+                                   input_act, input_act_weight, input_act_eps, residual, residual_scale)
+
+    def install_backend(strided_int8_matmul):
+        """Replace only Kitchen's eager int8_linear export, verified through
+        the registry; call between workloads."""
+        binding.install_backend(strided_int8_matmul, int8_linear)
+
+    def disable_backend():
+        """Restore the original export; refuses to overwrite another patch."""
+        binding.disable_backend(int8_linear)
+
+    @contextmanager
+    def kitchen_int8_without_transpose_copy(strided_int8_matmul):
+        """Scoped install; nested or concurrent contexts are rejected."""
+        with binding.scoped(strided_int8_matmul, int8_linear):
+            yield
+
+    return (int8_linear, install_backend, disable_backend, binding.get_stats, binding.reset_stats,
+            kitchen_int8_without_transpose_copy)
+
+
 _binding = KitchenInt8Binding()
-
-
-def int8_linear(x, weight, weight_scale, bias=None, out_dtype=torch.bfloat16, convrot=False,
-                convrot_groupsize=256, input_act=None, input_act_weight=None, input_act_eps=0.0,
-                residual=None, residual_scale=None):
-    """Pinned Kitchen eager INT8 linear semantics on the B200 kernels."""
-    return _binding.int8_linear(x, weight, weight_scale, bias, out_dtype, convrot, convrot_groupsize,
-                                input_act, input_act_weight, input_act_eps, residual, residual_scale)
-
-
-def install_backend(strided_int8_matmul):
-    _binding.install_backend(strided_int8_matmul, int8_linear)
-
-
-def disable_backend():
-    _binding.disable_backend(int8_linear)
-
-
-def get_stats():
-    return _binding.get_stats()
-
-
-def reset_stats():
-    _binding.reset_stats()
-
-
-@contextmanager
-def kitchen_int8_without_transpose_copy(strided_int8_matmul):
-    with _binding.scoped(strided_int8_matmul, int8_linear):
-        yield
+(int8_linear, install_backend, disable_backend, get_stats, reset_stats,
+ kitchen_int8_without_transpose_copy) = module_api(_binding)
