@@ -270,6 +270,26 @@ int b2_quant_linear_gather(int kind, const void* x, int x_dtype, int64_t M, int6
                            int64_t col0, int world, int rank, void* const* outs, void* const* states,
                            uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The same column-parallel linear with the transfer on the copy engines:
+ * the linear runs in `chunks` M-chunks (whole 256-row tiles, 1..8) on
+ * `stream`, each chunk's block going to every peer's output by one 2-D
+ * copy-engine copy on a per-peer copy stream while the next chunk is
+ * multiplied; when a peer's copies are done a one-thread kernel on the same
+ * copy stream adds 1 (release, system scope) to this rank's count in that
+ * peer's state, and `stream` joins the copy streams.  The caller then enqueues
+ * b2_gather_wait_ce, which advances this rank's sequence number and waits
+ * (bounded, 2 s, status 0x107) until every peer's count reaches it.  No
+ * per-call value: a step can be captured in a CUDA graph.  Same arguments and
+ * requirements as b2_quant_linear_gather minus `epoch`; calls on one device
+ * must not overlap (the copy streams and events are the library's, created
+ * once per device). */
+int b2_quant_linear_gather_ce(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
+                              const void* w, int64_t ldw, int64_t N, const float* w_scale, int64_t w_scale_count,
+                              const void* bias, int bias_dtype, int epilogue, int out_dtype, int64_t ldc,
+                              int64_t col0, int world, int rank, void* const* outs, void* const* states, int chunks,
+                              void* workspace, size_t workspace_bytes, void* stream);
+int b2_gather_wait_ce(void* state, int world, int rank, void* stream);
+
 /* Copy-engine copy of `rows` rows of `width_bytes` bytes between two device
  * buffers that may live on different GPUs (an IPC-mapped peer pointer, for
  * instance): the copy-engine counterpart of the gather, used to measure the

@@ -208,3 +208,164 @@ int b2_quant_linear_gather(int kind, const void* x, int x_dtype, int64_t M, int6
 }
 
 }  // extern "C"
+
+// ----------------------------------------------- copy-engine gather variant
+// The same column-parallel linear with the transfer done by the copy engines:
+// the linear runs in M-chunks on the caller's stream (prologue + plain pair
+// GEMM into this rank's columns of its own output); after each chunk, one
+// 2-D copy per peer, on a per-peer copy stream, carries the chunk's block
+// into that peer's output while the next chunk is multiplied.  When a peer's
+// copies are done a one-thread kernel on the same copy stream increments
+// this rank's count slot in the peer's state (system-scope release).  The
+// caller's stream then joins the copy streams and runs a bounded wait until
+// every peer's count reaches this call's sequence number, which the wait
+// kernel itself advances -- so nothing on the host depends on a per-call
+// value and a whole step can be captured in a CUDA graph and replayed.
+// The wait is its own entry point (b2_gather_wait_ce), enqueued after the
+// call; calls on one device must not overlap (they share the copy streams).
+namespace {
+
+constexpr int kCeCountOffset = 32;     // uint32 counts [world] (bytes 32..63)
+constexpr int kCeSeqOffset = 160;      // this rank's call sequence number
+constexpr int kCeMaxChunks = 8;
+
+struct CeStreams {
+  bool ready = false;
+  cudaStream_t copy[b2::kMaxGatherPeers];
+  cudaEvent_t chunk[kCeMaxChunks];
+  cudaEvent_t done[b2::kMaxGatherPeers];
+};
+CeStreams g_ce[64];
+std::mutex g_ce_mutex;
+
+cudaError_t ce_streams(CeStreams** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_ce_mutex);
+  CeStreams& c = g_ce[dev];
+  if (!c.ready) {
+    for (int i = 0; i < b2::kMaxGatherPeers; ++i) {
+      if ((e = cudaStreamCreateWithFlags(&c.copy[i], cudaStreamNonBlocking)) != cudaSuccess) return e;
+      if ((e = cudaEventCreateWithFlags(&c.done[i], cudaEventDisableTiming)) != cudaSuccess) return e;
+    }
+    for (int i = 0; i < kCeMaxChunks; ++i)
+      if ((e = cudaEventCreateWithFlags(&c.chunk[i], cudaEventDisableTiming)) != cudaSuccess) return e;
+    c.ready = true;
+  }
+  *out = &c;
+  return cudaSuccess;
+}
+
+__global__ void ce_signal_kernel(uint32_t* count_slot) {
+  __threadfence_system();
+  asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(count_slot) : "memory");
+}
+
+__global__ void ce_wait_kernel(uint32_t* state, int world, int rank, int* status) {
+  uint32_t* seq_slot = reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(state) + kCeSeqOffset);
+  const uint32_t* counts = reinterpret_cast<const uint32_t*>(reinterpret_cast<char*>(state) + kCeCountOffset);
+  const uint32_t seq = *seq_slot + 1u;  // only this kernel writes the slot, one launch at a time per stream
+  __syncthreads();
+  if (threadIdx.x == 0) *seq_slot = seq;
+  const int r = static_cast<int>(threadIdx.x);
+  if (r >= world || r == rank) return;
+  const uint64_t start = b2::globaltimer();
+  for (uint32_t i = 0;; ++i) {
+    if (static_cast<int32_t>(b2::ld_acquire_sys(counts + r) - seq) >= 0) return;
+    if ((i & 255u) == 255u && b2::globaltimer() - start > b2::kWaitLimitNs) {
+      if (status != nullptr) atomicCAS(status, 0, 0x100 | b2::kSiteGather);
+      return;
+    }
+    __nanosleep(100);
+  }
+}
+
+}  // namespace
+
+extern "C" int b2_quant_linear_gather_ce(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
+                                         int block, const void* w, int64_t ldw, int64_t N, const float* w_scale,
+                                         int64_t w_scale_count, const void* bias, int bias_dtype, int epilogue,
+                                         int out_dtype, int64_t ldc, int64_t col0, int world, int rank,
+                                         void* const* outs, void* const* states, int chunks, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  if (world < 1 || world > b2::kMaxGatherPeers + 1 || rank < 0 || rank >= world) return fail();
+  if (!outs || !states || chunks < 1 || chunks > kCeMaxChunks) return fail();
+  if (out_dtype != b2::kF16 && out_dtype != b2::kBF16 && out_dtype != b2::kF32) return fail();
+  const int ob = out_dtype == b2::kF32 ? 4 : 2;
+  if (col0 < 0 || col0 + N > ldc || (col0 * ob) % 16 != 0 || (ldc * ob) % 16 != 0) return fail();
+  for (int q = 0; q < world; ++q) {
+    if (!outs[q] || !aligned16(outs[q]) || !states[q]) return fail();
+    if (reinterpret_cast<uintptr_t>(states[q]) % 256 != 0) return fail();
+  }
+  char* own = static_cast<char*>(outs[rank]) + col0 * ob;
+  int st = b2::check_quant_linear(kind, x, x_dtype, M, K, ldx, block, w, ldw, N, w_scale, w_scale_count, bias,
+                                  bias_dtype, epilogue, own, out_dtype, ldc, workspace, workspace_bytes);
+  if (st != 0 || M == 0) return st;
+  CeStreams* cs = nullptr;
+  cudaError_t e = ce_streams(&cs);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t ldq = round_up(K, 16);
+  uint8_t* q = static_cast<uint8_t*>(workspace);
+  float* sa = reinterpret_cast<float*>(q + round_up(M * ldq, 256));
+  const int eb = x_dtype == b2::kF32 ? 4 : 2;
+  // chunks of whole 256-row pair tiles
+  int64_t rows = round_up((M + chunks - 1) / chunks, 256);
+  for (int64_t m0 = 0, c = 0; m0 < M; m0 += rows, ++c) {
+    const int64_t mc = M - m0 < rows ? M - m0 : rows;
+    e = b2::run_act_quant(static_cast<const char*>(x) + m0 * ldx * eb, x_dtype, mc, K, ldx, block,
+                          kind == b2::kKindE4M3 ? 1 : 0, q + m0 * ldq, ldq, sa + m0, s, /*early_dependents=*/true);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    b2::GemmParams p{};
+    p.M = static_cast<int>(mc);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.sa = sa + m0;
+    p.sb = w_scale;
+    p.sb_scalar = w_scale_count == 1 ? 1 : 0;
+    p.bias = bias;
+    p.bias_dtype = bias_dtype;
+    p.out = own + m0 * ldc * ob;
+    p.out_dtype = out_dtype;
+    p.ldc = ldc;
+    p.epilogue = epilogue;
+    p.vec_ok = 1;
+    p.weight_prefetch = 1;
+    if ((e = b2::run_qgemm(kind, q + m0 * ldq, ldq, w, ldw, p, 0, s)) != cudaSuccess) return static_cast<int>(e);
+    if (world == 1) continue;
+    if ((e = cudaEventRecord(cs->chunk[c], s)) != cudaSuccess) return static_cast<int>(e);
+    for (int r = 0, j = 0; r < world; ++r) {
+      if (r == rank) continue;
+      cudaStream_t cp = cs->copy[j++];
+      if ((e = cudaStreamWaitEvent(cp, cs->chunk[c], 0)) != cudaSuccess) return static_cast<int>(e);
+      char* dst = static_cast<char*>(outs[r]) + (m0 * ldc + col0) * ob;
+      if ((e = cudaMemcpy2DAsync(dst, static_cast<size_t>(ldc * ob), own + m0 * ldc * ob, static_cast<size_t>(ldc * ob),
+                                 static_cast<size_t>(N * ob), static_cast<size_t>(mc), cudaMemcpyDefault, cp)) !=
+          cudaSuccess)
+        return static_cast<int>(e);
+    }
+  }
+  if (world > 1) {
+    for (int r = 0, j = 0; r < world; ++r) {
+      if (r == rank) continue;
+      cudaStream_t cp = cs->copy[j];
+      uint32_t* slot = reinterpret_cast<uint32_t*>(static_cast<char*>(states[r]) + kCeCountOffset) + rank;
+      ce_signal_kernel<<<1, 1, 0, cp>>>(slot);
+      if ((e = cudaGetLastError()) != cudaSuccess) return static_cast<int>(e);
+      if ((e = cudaEventRecord(cs->done[j], cp)) != cudaSuccess) return static_cast<int>(e);
+      if ((e = cudaStreamWaitEvent(s, cs->done[j], 0)) != cudaSuccess) return static_cast<int>(e);
+      ++j;
+    }
+  }
+  return 0;
+}
+
+extern "C" int b2_gather_wait_ce(void* state, int world, int rank, void* stream) {
+  if (!state || world < 1 || world > b2::kMaxGatherPeers + 1 || rank < 0 || rank >= world) return fail();
+  if (reinterpret_cast<uintptr_t>(state) % 256 != 0) return fail();
+  ce_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint32_t*>(state), world, rank,
+                                                                  b2::status_word_ptr());
+  return static_cast<int>(cudaGetLastError());
+}

@@ -15,6 +15,10 @@ Reassembly of the full Y[M, N] on every rank, two ways:
   the multiplication tile by tile and Y arrives row-major with no permute
   pass.  Buffers come from a PeerGather, which maps every rank's buffers into
   every process once (CUDA IPC) and rotates through two of them.
+* ``gather="ce"``: the same buffers, the linear in M-chunks, and each
+  chunk's block carried to every peer by the copy engines while the next
+  chunk is multiplied (C ABI b2_quant_linear_gather_ce + b2_gather_wait_ce);
+  counter-based completion, so a step can be captured in a CUDA graph.
 * ``gather="nccl"``: the local linear, then one NCCL all_gather_into_tensor
   into [P, M, N/P] and a permute to [M, N] (any shard width, any local_fn).
 
@@ -44,6 +48,13 @@ def shard_range(n, world, rank, align=1):
     start = min(n, rank * per * align)
     stop = min(n, (rank + 1) * per * align)
     return start, stop
+
+
+def ce_chunks(world):
+    """M-chunks of the copy-engine gather: enough to overlap the transfer
+    with the GEMM while each rank's share of the GEMM is still large (4 at 2
+    ranks, 2 at 3-4); one chunk beyond, where the transfer dwarfs the GEMM."""
+    return 4 if world == 2 else 2 if world <= 4 else 1
 
 
 class PeerGather:
@@ -148,16 +159,17 @@ class ColumnParallelLinear:
         self.n_shard = n_total // self.world
         if w_shard.shape[0] != self.n_shard:
             raise ValueError("weight shard does not match N / world")
-        if gather not in ("auto", "peer", "nccl"):
-            raise ValueError("gather must be 'auto', 'peer' or 'nccl'")
+        if gather not in ("auto", "peer", "ce", "nccl"):
+            raise ValueError("gather must be 'auto', 'peer', 'ce' or 'nccl'")
         self.w, self.sw, self.bias = w_shard, w_scale_shard, bias_shard
         self.kw = dict(rotation_block=rotation_block, out_dtype=out_dtype, epilogue=epilogue, kind=kind)
         self.local_fn = local_fn or (lambda x, w, sw, b: w8a8_linear(x, w, sw, b, **self.kw))
         peer_ok = local_fn is None and self.n_shard % 64 == 0 and kind in ("int8", "e4m3")
-        if gather == "peer" and not peer_ok:
-            raise ValueError("the peer gather needs the built-in linear and N / world % 64 == 0")
-        self.gather_mode = "peer" if (gather == "peer" or (gather == "auto" and peer_ok and peers is not None)) \
-            else "nccl"
+        if gather in ("peer", "ce") and not peer_ok:
+            raise ValueError("the peer and copy-engine gathers need the built-in linear and N / world % 64 == 0")
+        if gather == "auto":
+            gather = "ce" if (peer_ok and peers is not None) else "nccl"
+        self.gather_mode = gather
         self.peers = peers
         self._workspace = None
 
@@ -203,18 +215,23 @@ class ColumnParallelLinear:
             raise ValueError("weight shard rows must be 16-byte aligned")
         kind = nat.KIND_I8 if self.kw["kind"] == "int8" else nat.KIND_E4M3
         stream = nat.stream_ptr(dev)
-        nat.check(lib.b2_quant_linear_gather(
-            kind, x2.data_ptr(), nat.DTYPE_CODE[x.dtype], m, k, x2.stride(0) if m > 1 else k,
-            _block(self.kw["rotation_block"], k), w_t.data_ptr(), ldw, self.n_shard, self.sw.data_ptr(),
-            self.sw.numel(), nat.ptr(self.bias), nat.DTYPE_CODE[self.bias.dtype] if self.bias is not None else 0,
-            EPILOGUES[self.kw["epilogue"]], nat.DTYPE_CODE[out_dtype], self.n_total, self.rank * self.n_shard,
-            self.world, self.rank, g.outs[slot], g.states, epoch, self._workspace.data_ptr(),
-            self._workspace.numel(), stream), "b2_quant_linear_gather")
-        g.wait(epoch, stream)
+        common = (kind, x2.data_ptr(), nat.DTYPE_CODE[x.dtype], m, k, x2.stride(0) if m > 1 else k,
+                  _block(self.kw["rotation_block"], k), w_t.data_ptr(), ldw, self.n_shard, self.sw.data_ptr(),
+                  self.sw.numel(), nat.ptr(self.bias), nat.DTYPE_CODE[self.bias.dtype] if self.bias is not None else 0,
+                  EPILOGUES[self.kw["epilogue"]], nat.DTYPE_CODE[out_dtype], self.n_total, self.rank * self.n_shard,
+                  self.world, self.rank, g.outs[slot], g.states)
+        if self.gather_mode == "ce":
+            nat.check(lib.b2_quant_linear_gather_ce(*common, ce_chunks(self.world), self._workspace.data_ptr(),
+                                                    self._workspace.numel(), stream), "b2_quant_linear_gather_ce")
+            nat.check(lib.b2_gather_wait_ce(g.state.data_ptr(), self.world, self.rank, stream), "b2_gather_wait_ce")
+        else:
+            nat.check(lib.b2_quant_linear_gather(*common, epoch, self._workspace.data_ptr(), self._workspace.numel(),
+                                                 stream), "b2_quant_linear_gather")
+            g.wait(epoch, stream)
         return y.reshape(*x.shape[:-1], self.n_total)
 
     def forward(self, x, gather=True):
-        if gather and self.gather_mode == "peer":
+        if gather and self.gather_mode in ("peer", "ce"):
             return self._forward_peer(x)
         y = self.forward_local(x)
         if not gather or self.world == 1:
