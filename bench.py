@@ -55,6 +55,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sustained", action="store_true", help="skip the >= 1 s sustained leg (profiling runs)")
     ap.add_argument("--sets", type=int, default=4, help="input sets cycled to defeat L2 reuse")
+    ap.add_argument("--gather", choices=("fused", "ce"), default="fused",
+                    help="N > 1 step: gather by SM peer stores in the GEMM epilogue (fused) or by copy engines "
+                         "overlapped with a chunked GEMM (ce)")
+    ap.add_argument("--gather-store", choices=("auto", "sm", "tma"), default="auto",
+                    help="transport of the fused gather's peer copies: SM stores or TMA stores")
     ap.add_argument("--column-parallel", action="store_true",
                     help="c5 on one GPU through the column-parallel stack (the N > 1 code path, eager calls)")
     ap.add_argument("--workload", default="c2",
@@ -542,11 +547,12 @@ def run_b200_multi(args, rank, world, local_rank):
     import rdna2_ops
     from rdna2_ops import _native as nat
     from rdna2_ops import qlinear
-    from rdna2_ops.column_parallel import PeerGather
+    from rdna2_ops.column_parallel import PeerGather, ce_chunks, set_gather_store
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     lib = nat.library()
+    set_gather_store(args.gather_store)
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
     gen = torch.Generator(device=dev)
@@ -585,6 +591,9 @@ def run_b200_multi(args, rank, world, local_rank):
         return run_b200_multi_nccl(args, rank, world, local_rank, xs, wq_full, sw_full, bias_full,
                                    peer_error or "a peer rank could not map the gather buffers")
 
+    def barrier():
+        dist.barrier(device_ids=[local_rank])
+
     def gather_step(i, w_rows, sw_rows, b_rows, n_total, col0):
         s = i % args.sets
         epoch, slot = g.next_slot()
@@ -598,11 +607,23 @@ def run_b200_multi(args, rank, world, local_rank):
         g.wait(epoch, sptr)
         return slot
 
-    def strong(i):
-        return gather_step(i, wqs, sw, bias, N, c0)
+    def gather_step_ce(i, w_rows, sw_rows, b_rows, n_total, col0, chunks):
+        s = i % args.sets
+        _, slot = g.next_slot()
+        st = lib.b2_quant_linear_gather_ce(nat.KIND_I8, xs[s].data_ptr(), nat.F16, M, K, K, ROT,
+                                           w_rows[s].data_ptr(), K, w_rows[s].shape[0], sw_rows.data_ptr(),
+                                           sw_rows.numel(), b_rows.data_ptr(), nat.F16, nat.EPI_SEPARATE, nat.F16,
+                                           n_total, col0, world, rank, g.outs[slot], g.states, chunks,
+                                           ws.data_ptr(), ws_bytes, sptr)
+        if st:
+            nat.check(st, "b2_quant_linear_gather_ce")
+        nat.check(lib.b2_gather_wait_ce(g.state.data_ptr(), world, rank, sptr), "b2_gather_wait_ce")
+        return slot
 
-    def barrier():
-        dist.barrier(device_ids=[local_rank])
+    def strong(i):
+        if args.gather == "ce":
+            return gather_step_ce(i, wqs, sw, bias, N, c0, ce_chunks(world))
+        return gather_step(i, wqs, sw, bias, N, c0)
 
     def timed(fn, steps, sample_clocks=False):
         barrier()
@@ -624,11 +645,15 @@ def run_b200_multi(args, rank, world, local_rank):
         return _max_over_ranks(torch, dist, dev, e0.elapsed_time(e1) / steps), t_wall, sampler
 
     # ---- correctness once: every rank holds the whole single-GPU result
-    slot = strong(0)
-    torch.cuda.synchronize()
     ref = rdna2_ops.w8a8_linear(xs[0], wq_full, sw_full, bias_full, rotation_block=ROT, out_dtype=torch.float16)
-    got = g.local[slot][: M * N].view(M, N)
-    assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), "gathered output differs from 1-GPU linear"
+    for check in (lambda: gather_step(0, wqs, sw, bias, N, c0),
+                  lambda: gather_step_ce(0, wqs, sw, bias, N, c0, ce_chunks(world))):
+        slot = check()
+        torch.cuda.synchronize()
+        got = g.local[slot][: M * N].view(M, N)
+        assert torch.equal(got.view(torch.int16), ref.view(torch.int16)), "gathered output differs from 1-GPU linear"
+        g.local[slot].fill_(0)
+        barrier()
     del ref, wq_full
     for i in range(max(3, args.warmup)):
         strong(i)
@@ -688,6 +713,21 @@ def run_b200_multi(args, rank, world, local_rank):
     for i in range(3):
         ce_gather(i)
     ce_ms, _, _ = timed(ce_gather, max(10, n_side // 4))
+    # the other gather variant's step, and the copy-engine step by chunk count
+    other = {}
+    for store in ("sm", "tma"):
+        set_gather_store(store)
+        for i in range(3):
+            gather_step(i, wqs, sw, bias, N, c0)
+        other[f"fused_gather_step_ms_{store}_stores"], _, _ = timed(lambda i: gather_step(i, wqs, sw, bias, N, c0),
+                                                                   n_side)
+    set_gather_store(args.gather_store)
+    for ch in (1, 2, 4, 8):
+        def step_ch(i, ch=ch):
+            return gather_step_ce(i, wqs, sw, bias, N, c0, ch)
+        for i in range(3):
+            step_ch(i)
+        other[f"ce_gather_step_ms_chunks{ch}"], _, _ = timed(step_ch, n_side)
     # end to end: X uploaded to every rank, the rank's columns computed by the
     # public call and read back over the rank's own PCIe link; the host holds
     # Y by column shards (no device gather: the consumer is the host)
@@ -721,6 +761,17 @@ def run_b200_multi(args, rank, world, local_rank):
     int8_peak = 2.0 * pk["bf16_tflops"]
     nvlink_gbs = 770.0
     recv = (world - 1) * M * ns * 2                   # bytes every rank must receive per step
+    if args.gather == "ce":
+        rows = -(-(-(-M // ce_chunks(world))) // 256) * 256
+        n_chunks = -(-M // rows)
+        launches = 2 * n_chunks + (world - 1) + 1     # prologue + GEMM per chunk, a signal per peer, the wait
+        gather_desc = (f"copy engines: the linear in {n_chunks} M-chunks, one 2-D copy per peer and chunk on "
+                       "per-peer copy streams overlapping the next chunk's GEMM, counter signal + bounded wait")
+    else:
+        launches = 3                                  # prologue, GEMM with peer-store epilogue, wait
+        gather_desc = ("fused: peer copies from the GEMM epilogue ("
+                       + ("TMA stores" if args.gather_store == "tma" else "SM stores")
+                       + ") + epoch flags + bounded wait")
     t_gemm = 2.0 * M * ns * K / (int8_peak * 1e12) * 1e3
     t_link = recv / (nvlink_gbs * 1e9) * 1e3
     target = max(t_gemm, t_link)
@@ -743,7 +794,8 @@ def run_b200_multi(args, rank, world, local_rank):
                        "every GPU, each rank's N/P columns back over its own PCIe link; uploads / linear / "
                        "read-backs on three streams, double buffered",
                 "ms_per_step": round(e2e_ms, 4)},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": launches * args.steps,
+        "gather": gather_desc,
         "clocks": clocks.summary(),
         "device_status": status,
         "wall_s_timed": round(t_wall, 4),
@@ -760,7 +812,10 @@ def run_b200_multi(args, rank, world, local_rank):
             "copy_engine_gather_gbs_per_rank": round(recv / (ce_ms * 1e-3) / 1e9, 1),
             "copy_engine_note": "each rank's [M, N/P] block copied to every peer's Y by 2-D copy-engine "
                                 "copies, one stream per peer, no GEMM: the link bandwidth measured in this run",
-            "fused_gather_gbs_per_rank": round(recv / (ms * 1e-3) / 1e9, 1),
+            "step_gather_gbs_per_rank": round(recv / (ms * 1e-3) / 1e9, 1),
+            **{k_: round(v_, 5) for k_, v_ in other.items()},
+            "ce_note": "b2_quant_linear_gather_ce: the linear in M-chunks, each chunk's block copied to every "
+                       "peer by the copy engines while the next chunk is multiplied; counter completion",
         },
     }
     print(json.dumps(line), flush=True)
@@ -842,10 +897,11 @@ def run_c5_multi(args, rank, world, local_rank):
     import torch.distributed as dist
     from rdna2_ops import _native as nat
     from rdna2_ops import qlinear
-    from rdna2_ops.column_parallel import ColumnParallelStack, PeerGather
+    from rdna2_ops.column_parallel import ColumnParallelStack, PeerGather, ce_chunks, set_gather_store
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
+    set_gather_store(args.gather_store)
     stream = torch.cuda.current_stream(dev)
     gen = torch.Generator(device=dev)
     gen.manual_seed(SEED)
@@ -861,7 +917,7 @@ def run_c5_multi(args, rank, world, local_rank):
         blocks.append(blk)
     x0 = torch.randn((m, hid), generator=gen, device=dev).half()
     g = PeerGather(m * 4 * hid, torch.float16)
-    stack = ColumnParallelStack(blocks, peers=g, gather="peer")
+    stack = ColumnParallelStack(blocks, peers=g, gather="ce" if args.gather == "ce" else "peer")
     del blocks
     torch.cuda.empty_cache()
 
@@ -894,6 +950,11 @@ def run_c5_multi(args, rank, world, local_rank):
         return
     flops = 2.0 * m * sum(n_ * k_ for n_, k_ in shapes) * nblocks
     recv = (world - 1) / world * m * sum(n_ for n_, _ in shapes) * 2 * nblocks
+    if args.gather == "ce":
+        rows = -(-(-(-m // ce_chunks(world))) // 256) * 256
+        stack_launches = 4 * nblocks * (2 * -(-m // rows) + (world - 1 if world > 1 else 0) + 1)
+    else:
+        stack_launches = 3 * 4 * nblocks
     line = {"workload": "c5", "metric": "W8A8 DiT stack TOPS (config 5, 28 blocks, rotated)",
             "value": round(flops / (ms * 1e-3) / 1e12, 2), "unit": "TOPS", "n_gpus": world, "steps": steps,
             "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True,
@@ -902,13 +963,16 @@ def run_c5_multi(args, rank, world, local_rank):
                        "linears": "QKV 9216x3072, out 3072x3072 (on the Q third), up 12288x3072, down 3072x12288, "
                                   "block-128 rotation, every weight N-sharded over the ranks",
                        "parallelism": f"column-parallel x{world}, every layer output gathered to every rank "
-                                      "inside the GEMM epilogue (NVLink peer stores)"},
+                                      + ("by copy engines overlapping a chunked GEMM" if args.gather == "ce"
+                                         else "inside the GEMM epilogue (NVLink peer stores)")},
             "roofline": {"bound": "nvlink", "nvlink_bytes_received_per_rank": int(recv),
                          "link_floor_ms": round(recv / 770e9 * 1e3, 3),
                          "gemm_floor_ms": round(flops / world / (2.0 * peaks()["bf16_tflops"] * 1e12) * 1e3, 3),
                          "frac": round(max(recv / 770e9 * 1e3,
                                            flops / world / (2.0 * peaks()["bf16_tflops"] * 1e12) * 1e3) / ms, 4)},
-            "gpu_launches": 3 * 4 * nblocks * steps, "clocks": clocks.summary(), "device_status": status,
+            "gpu_launches": stack_launches * steps, "gather": args.gather,
+            "gather_store": args.gather_store if args.gather != "ce" else None, "clocks": clocks.summary(),
+            "device_status": status,
             "timing": "eager public ColumnParallelStack calls"}
     print(json.dumps(line), flush=True)
 

@@ -80,6 +80,14 @@ int b2_set_prologue_path(int path);
  * tensor core's fp32 summation order.  No reference counterpart. */
 int b2_set_w4a16_path(int path);
 
+/* Process-wide transport of the fused column-parallel gather
+ * (b2_quant_linear_gather): 0 = default (1), 1 = each staged 32-row output
+ * unit copied to every peer by 16-byte SM stores from the epilogue warps,
+ * 2 = by TMA stores through one tensor map per peer output.  Outputs,
+ * flags and completion rules are identical for every choice.  No reference
+ * counterpart. */
+int b2_set_gather_store(int mode);
+
 /* SYNCHRONOUS: read (and if reset != 0 clear) the device status word that a
  * kernel sets when one of its bounded waits gives up (0 = no failure; else
  * 0x100 | site).  Call after synchronizing the stream. */

@@ -413,6 +413,12 @@ __device__ __forceinline__ void bulk_wait_read() {
 // Every bulk group of the issuing thread has completed.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Orders this thread's completed async-proxy (TMA) global writes before its
+// later generic-proxy memory operations (a fence and a flag release).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Contiguous global -> shared bulk copy (no tensor map, no multicast),
 // completing on `bar`.  Both addresses 16-byte aligned, bytes % 16 == 0.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -8,6 +8,12 @@ namespace b2 {
 
 // Most peers one column-parallel gather writes to (8 GPUs per node).
 constexpr int kMaxGatherPeers = 7;
+// GemmParams::gather: 0 = no gather; peer copies of each staged output unit
+// by 16-byte SM stores (kGatherSm) or by TMA stores through per-peer tensor
+// maps (kGatherTma).
+constexpr int kGatherSm = 1;
+constexpr int kGatherTma = 2;
+constexpr int kGatherDefault = kGatherSm;
 
 struct GemmParams {
   int M, N, K;
@@ -64,6 +70,7 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
 
 // 0 = automatic, 1 = single-CTA kernel only, 2 = 2-CTA pair kernel only.
 void set_gemm_path(int path);
+void set_gather_store(int mode);
 void set_prologue_path(int path);
 void set_w4a16_path(int path);
 int pair_capacity();

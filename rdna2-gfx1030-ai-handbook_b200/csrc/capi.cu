@@ -102,6 +102,12 @@ int b2_set_w4a16_path(int path) {
   return 0;
 }
 
+int b2_set_gather_store(int mode) {
+  if (mode < 0 || mode > 2) return fail();
+  b2::set_gather_store(mode);
+  return 0;
+}
+
 int b2_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block, int quant,
                  void* q, int64_t ldq, float* scale, void* stream) {
   if (M < 0 || K < 1 || M > INT32_MAX || K > 16384) return fail();

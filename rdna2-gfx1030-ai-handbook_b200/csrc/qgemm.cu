@@ -320,6 +320,17 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, uint32_t tadd
   }
 }
 
+// Tensor maps of the peers' outputs (same geometry as this rank's output
+// map, other base addresses), a kernel parameter of the gather kernels only.
+template <bool GATHER>
+struct PeerMaps {
+  CUtensorMap m[kMaxGatherPeers];
+};
+template <>
+struct PeerMaps<false> {
+  int unused;
+};
+
 // Column-parallel gather: copy one staged unit (32 rows x 128 bytes at
 // `buf`, 128-byte swizzle) to every peer output with 16-byte stores, four
 // whole 128-byte row segments per warp instruction.  Gather mode requires
@@ -367,9 +378,10 @@ __device__ __forceinline__ void gather_signal(const GemmParams& p) {
 // unit is converted.  Lane 0 issues and waits on the warp's bulk groups; the
 // tensor map clips rows >= M and columns >= N.
 template <int KIND, int BN, bool GATHER, typename Release>
-__device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const CUtensorMap* tma_c, uint32_t taddr,
-                                                  int row, int row0, int n0, int lane, float* wst,
-                                                  uint32_t obuf, uint32_t& ob_sel, Release release) {
+__device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const CUtensorMap* tma_c,
+                                                  const PeerMaps<GATHER>* pm, uint32_t taddr, int row, int row0,
+                                                  int n0, int lane, float* wst, uint32_t obuf, uint32_t& ob_sel,
+                                                  Release release) {
   constexpr int NC = BN / 32;
   static_assert(NC % 2 == 0, "ping-pong over chunk pairs");
   const int uc = (p.out_dtype == kF16 || p.out_dtype == kBF16) ? 2 : 1;  // chunks per staging row
@@ -389,9 +401,15 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const CUt
       const int x = n0 + (c - part) * 32;
       if (lane == 0 && row0 < p.M && x < p.N) {
         tma_store_2d(tma_c, buf, x, row0);
+        if constexpr (GATHER) {
+          if (p.gather == kGatherTma)
+            for (int q = 0; q < p.n_peers; ++q) tma_store_2d(&pm->m[q], buf, x, row0);
+        }
         bulk_commit_group();
       }
-      if constexpr (GATHER) peer_store_unit(p, buf, row0, x, lane);
+      if constexpr (GATHER) {
+        if (p.gather != kGatherTma) peer_store_unit(p, buf, row0, x, lane);
+      }
       ob_sel ^= 1u;
     }
   };
@@ -593,7 +611,8 @@ template <int KIND, int BN, int STAGES, bool TSTORE, bool GATHER = false>
 __global__ void __launch_bounds__(192, 1)
     qgemm_pair_kernel(const __grid_constant__ CUtensorMap tma_a,
                       const __grid_constant__ CUtensorMap tma_b,
-                      const __grid_constant__ CUtensorMap tma_c, const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tma_c,
+                      const __grid_constant__ PeerMaps<GATHER> peer_maps, const GemmParams p) {
   using L = Smem<128, BN / 2, BN, STAGES, TSTORE ? kOutStageBytes : 0>;
   constexpr int kKbElems = (KIND == kKindBF16 || KIND == kKindF16) ? 64 : 128;
   extern __shared__ uint8_t smem_raw[];
@@ -744,14 +763,17 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) mbar_arrive_cluster(tempty_leader + static_cast<uint32_t>(buf * 8));
       };
       if constexpr (TSTORE) {
-        epilogue_tile_tma<KIND, BN, GATHER>(p, &tma_c, taddr, row0 + lane, row0, tn * BN, lane, wsb, obuf,
-                                            ob_sel, release);
+        epilogue_tile_tma<KIND, BN, GATHER>(p, &tma_c, &peer_maps, taddr, row0 + lane, row0, tn * BN, lane, wsb,
+                                            obuf, ob_sel, release);
       } else {
         epilogue_tile<KIND, BN>(p, taddr, row0 + lane, tn * BN, lane, wsb, release);
       }
     }
     if constexpr (TSTORE) {
-      if (lane == 0) bulk_wait_all();  // staging reads and global writes done
+      if (lane == 0) {
+        bulk_wait_all();  // staging reads and global writes (this GPU's and the peers') done
+        if constexpr (GATHER) fence_proxy_async_global();
+      }
       __syncwarp();
     }
     if constexpr (GATHER) gather_signal(p);
@@ -1179,10 +1201,17 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
   if ((e = make_kmajor_map(&mb, b, eb, p.K, p.N, ldb * eb, BN / 2)) != cudaSuccess) return e;
   CUtensorMap mc;
   memset(&mc, 0, sizeof(mc));
+  PeerMaps<GATHER> pm;
+  memset(&pm, 0, sizeof(pm));
   if (TSTORE) {
     const int ob = (p.out_dtype == kF16 || p.out_dtype == kBF16) ? 2 : 4;
     if (!p.vec_ok) return cudaErrorInvalidValue;
     if ((e = make_out_map(&mc, p.out, ob, p.N, p.M, p.ldc * ob)) != cudaSuccess) return e;
+    if constexpr (GATHER) {
+      if (p.gather == kGatherTma)
+        for (int q = 0; q < p.n_peers; ++q)
+          if ((e = make_out_map(&pm.m[q], p.peer_out[q], ob, p.N, p.M, p.ldc * ob)) != cudaSuccess) return e;
+    }
   }
   p.tiles_m = static_cast<int>((p.M + 255) / 256);
   p.tiles_n = static_cast<int>((p.N + BN - 1) / BN);
@@ -1192,7 +1221,7 @@ static cudaError_t launch_pair(const void* a, int64_t lda, const void* b, int64_
   if (tiles < pairs) pairs = tiles;
   cfg.gridDim = dim3(2 * pairs);
   cfg.numAttrs = 2;
-  e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, p);
+  e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, pm, p);
   return e != cudaSuccess ? e : cudaGetLastError();
 }
 
@@ -1307,6 +1336,7 @@ static int choose_config(int64_t M, int64_t N) {
 // 8 split-K swap-AB cluster kernel (M <= 32 only); 9 pair BN=192 with the
 // TMA-store epilogue.
 static int g_force_path = 0;
+static int g_gather_store = 0;  // 0 = default, else kGatherSm / kGatherTma
 
 template <int KIND>
 static cudaError_t dispatch(int cfg, const void* a, int64_t lda, const void* b, int64_t ldb,
@@ -1334,6 +1364,8 @@ static cudaError_t run_gather(int kind, const void* a, int64_t lda, const void* 
                               const GemmParams& p, cudaStream_t stream) {
   if (!p.vec_ok || p.N % 64 != 0 || p.n_peers < 0 || p.n_peers > kMaxGatherPeers || !p.done_count)
     return cudaErrorInvalidValue;
+  GemmParams q = p;
+  q.gather = g_gather_store == 0 ? kGatherDefault : g_gather_store;
   const int pairs = pair_capacity();
   if (pairs <= 0) return cudaErrorNotSupported;
   const int64_t tm2 = (p.M + 255) / 256;
@@ -1341,11 +1373,11 @@ static cudaError_t run_gather(int kind, const void* a, int64_t lda, const void* 
   const int64_t w192 = (tm2 * ((p.N + 191) / 192) + pairs - 1) / pairs;
   const bool narrow = static_cast<double>(w192) * 192.0 * 1.06 < static_cast<double>(w256) * 256.0;
   if (kind == kKindI8)
-    return narrow ? launch_pair<kKindI8, 192, 6, true, true>(a, lda, b, ldb, p, 0, stream)
-                  : launch_pair<kKindI8, 256, 6, true, true>(a, lda, b, ldb, p, 0, stream);
+    return narrow ? launch_pair<kKindI8, 192, 6, true, true>(a, lda, b, ldb, q, 0, stream)
+                  : launch_pair<kKindI8, 256, 6, true, true>(a, lda, b, ldb, q, 0, stream);
   if (kind == kKindE4M3)
-    return narrow ? launch_pair<kKindE4M3, 192, 6, true, true>(a, lda, b, ldb, p, 0, stream)
-                  : launch_pair<kKindE4M3, 256, 6, true, true>(a, lda, b, ldb, p, 0, stream);
+    return narrow ? launch_pair<kKindE4M3, 192, 6, true, true>(a, lda, b, ldb, q, 0, stream)
+                  : launch_pair<kKindE4M3, 256, 6, true, true>(a, lda, b, ldb, q, 0, stream);
   return cudaErrorInvalidValue;
 }
 
@@ -1401,6 +1433,8 @@ cudaError_t run_qgemm(int kind, const void* a, int64_t lda, const void* b, int64
 }
 
 void set_gemm_path(int path) { g_force_path = path; }
+
+void set_gather_store(int mode) { g_gather_store = mode; }
 
 }  // namespace b2
 

@@ -34,6 +34,7 @@ SIGNATURES = {
     "b2_set_gemm_path": ([_int], _int),
     "b2_set_prologue_path": ([_int], _int),
     "b2_set_w4a16_path": ([_int], _int),
+    "b2_set_gather_store": ([_int], _int),
     "b2_pair_capacity": ([], _int),
     "b2_device_status": ([ctypes.POINTER(_int), _int], _int),
     "b2_act_quant": ([_p, _int, _i64, _i64, _i64, _int, _int, _p, _i64, _p, _p], _int),

@@ -50,11 +50,21 @@ def shard_range(n, world, rank, align=1):
     return start, stop
 
 
+def set_gather_store(mode):
+    """Transport of the fused gather's peer copies, process-wide: "auto",
+    "sm" (16-byte stores from the epilogue warps) or "tma" (TMA stores
+    through per-peer tensor maps).  Outputs are identical for every choice."""
+    codes = {"auto": 0, "sm": 1, "tma": 2}
+    if mode not in codes:
+        raise ValueError("gather store must be 'auto', 'sm' or 'tma'")
+    nat.check(nat.library().b2_set_gather_store(codes[mode]), "b2_set_gather_store")
+
+
 def ce_chunks(world):
     """M-chunks of the copy-engine gather: enough to overlap the transfer
     with the GEMM while each rank's share of the GEMM is still large (4 at 2
     ranks, 2 at 3-4); one chunk beyond, where the transfer dwarfs the GEMM."""
-    return 4 if world == 2 else 2 if world <= 4 else 1
+    return 1 if world == 1 else 4 if world == 2 else 2 if world <= 4 else 1
 
 
 class PeerGather:
@@ -168,7 +178,7 @@ class ColumnParallelLinear:
         if gather in ("peer", "ce") and not peer_ok:
             raise ValueError("the peer and copy-engine gathers need the built-in linear and N / world % 64 == 0")
         if gather == "auto":
-            gather = "ce" if (peer_ok and peers is not None) else "nccl"
+            gather = "peer" if (peer_ok and peers is not None) else "nccl"
         self.gather_mode = gather
         self.peers = peers
         self._workspace = None

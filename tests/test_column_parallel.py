@@ -162,13 +162,16 @@ def _peer_worker(rank, world, port, q):
         wq, sw = qlinear.quantize_weight(w, rotation_block=128)
         bias = (torch.randn(n, generator=gen, device="cuda") * 0.02).half()
         g = PeerGather(8192 * 2048, torch.float16)
-        layer = ColumnParallelLinear.from_full(wq, sw, bias, rotation_block=128, out_dtype=torch.float16,
-                                               gather="peer", peers=g)
         ref = w8a8_linear(x, wq, sw, bias, rotation_block=128, out_dtype=torch.float16)
         ok = True
-        for _ in range(5):                      # both ring buffers, several epochs
-            y = layer(x)
-            ok &= bool(torch.equal(y.view(torch.int16), ref.view(torch.int16)))
+        from rdna2_ops.column_parallel import set_gather_store
+        for mode, store in (("peer", "sm"), ("ce", "auto"), ("peer", "tma"), ("ce", "auto"), ("peer", "auto")):
+            set_gather_store(store)                 # every variant, interleaved on the same buffers
+            layer = ColumnParallelLinear.from_full(wq, sw, bias, rotation_block=128, out_dtype=torch.float16,
+                                                   gather=mode, peers=g)
+            for _ in range(5):                      # both ring buffers, several calls
+                y = layer(x)
+                ok &= bool(torch.equal(y.view(torch.int16), ref.view(torch.int16)))
         # two DiT blocks (hidden 512), column-parallel with the peer gather,
         # against the same chain of single-GPU fused linears
         hid, blocks = 512, []
@@ -186,9 +189,12 @@ def _peer_worker(rank, world, port, q):
             o = w8a8_linear(qkv[:, :hid], q2, s2, rotation_block=128, out_dtype=torch.float16)
             yr = w8a8_linear(w8a8_linear(o, q3, s3, rotation_block=128, out_dtype=torch.float16), q4, s4,
                              rotation_block=128, out_dtype=torch.float16)
-        stack = ColumnParallelStack(blocks, peers=g, gather="peer")
-        ys = stack(x0)
-        ok_stack = bool(torch.equal(ys.view(torch.int16), yr.view(torch.int16)))
+        ok_stack = True
+        for mode, store in (("peer", "sm"), ("peer", "tma"), ("ce", "auto")):
+            set_gather_store(store)
+            stack = ColumnParallelStack(blocks, peers=g, gather=mode)
+            ys = stack(x0)
+            ok_stack &= bool(torch.equal(ys.view(torch.int16), yr.view(torch.int16)))
         from rdna2_ops import _native as nat
         q.put((rank, ok, ok_stack, nat.device_status()))
     finally:
@@ -201,8 +207,9 @@ def _peer_worker(rank, world, port, q):
 @pytest.mark.gpu
 def test_peer_gather_column_parallel_bit_identical():
     """Every rank's reassembled output (the gather inside the GEMM epilogue,
-    over NVLink) equals the single-GPU fused linear bit for bit, over several
-    epochs; a 2-block column-parallel DiT stack equals the 1-GPU stack."""
+    or by copy engines behind a chunked GEMM, over NVLink) equals the
+    single-GPU fused linear bit for bit, over several calls; a 2-block
+    column-parallel DiT stack equals the 1-GPU stack with either gather."""
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs 2 GPUs")

@@ -1,7 +1,7 @@
 """The fused column-parallel gather (b2_quant_linear_gather + b2_gather_wait)
 on ONE GPU: P "virtual ranks" run one after another on one stream, each
 rank's peer buffers being other buffers of the same device.  Every peer
-store, flag slot, CTA count and bounded wait of the multi-GPU path runs as
+store (SM stores or TMA stores through per-peer tensor maps), flag slot, CTA count and bounded wait of the multi-GPU path runs as
 it does across GPUs; only the IPC mapping is absent.  Every rank's full
 output must equal the single-GPU fused linear of the whole weight bit for
 bit (per-token scales see the whole row on every rank), over repeated
@@ -30,6 +30,15 @@ def _status():
     nat.device_status(reset=True)
     yield
     assert nat.device_status() == 0
+
+
+@pytest.fixture(params=["sm", "tma"])
+def store(request):
+    """Both transports of the fused gather's peer copies."""
+    from rdna2_ops.column_parallel import set_gather_store
+    set_gather_store(request.param)
+    yield request.param
+    set_gather_store("auto")
 
 
 class VirtualRanks:
@@ -76,7 +85,7 @@ def _run_all_ranks(vr, epoch, x, wq, sw, bias, block, kind, epilogue, out_dtype)
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 @pytest.mark.parametrize("m,n_total,k,block", [(300, 1536, 512, 128), (4096, 12288, 3072, 128),
                                                (1, 512, 256, None), (513, 3072, 1024, 256)])
-def test_gather_equals_single_gpu_linear(world, m, n_total, k, block):
+def test_gather_equals_single_gpu_linear(world, m, n_total, k, block, store):
     rng = np.random.default_rng(world * 7 + m)
     x = torch.from_numpy(outlier_activations(rng, m, k)).half().cuda()
     w = torch.from_numpy((rng.standard_normal((n_total, k)) * 0.02).astype(np.float32)).cuda()
@@ -98,7 +107,7 @@ def test_gather_equals_single_gpu_linear(world, m, n_total, k, block):
 @pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("epilogue", ["separate", "fused", "kitchen"])
 @pytest.mark.parametrize("kind", ["int8", "e4m3"])
-def test_gather_dtypes_and_kinds(out_dtype, epilogue, kind):
+def test_gather_dtypes_and_kinds(out_dtype, epilogue, kind, store):
     world, m, n_total, k = 4, 700, 2048, 768
     rng = np.random.default_rng(11)
     x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).to(torch.bfloat16).cuda()
