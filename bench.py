@@ -60,6 +60,9 @@ def parse():
                          "overlapped with a chunked GEMM (ce)")
     ap.add_argument("--gather-store", choices=("auto", "sm", "tma"), default="auto",
                     help="transport of the fused gather's peer copies: SM stores or TMA stores")
+    ap.add_argument("--activations", choices=("fp16", "int8"), default="fp16",
+                    help="c5 column-parallel stack: gather every fp16 layer output, or exchange only the next "
+                         "layer's INT8 input codes")
     ap.add_argument("--column-parallel", action="store_true",
                     help="c5 on one GPU through the column-parallel stack (the N > 1 code path, eager calls)")
     ap.add_argument("--workload", default="c2",
@@ -897,7 +900,8 @@ def run_c5_multi(args, rank, world, local_rank):
     import torch.distributed as dist
     from rdna2_ops import _native as nat
     from rdna2_ops import qlinear
-    from rdna2_ops.column_parallel import ColumnParallelStack, PeerGather, ce_chunks, set_gather_store
+    from rdna2_ops.column_parallel import (ActivationExchange, ColumnParallelStack, PeerGather, ce_chunks,
+                                           set_gather_store)
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -917,7 +921,12 @@ def run_c5_multi(args, rank, world, local_rank):
         blocks.append(blk)
     x0 = torch.randn((m, hid), generator=gen, device=dev).half()
     g = PeerGather(m * 4 * hid, torch.float16)
-    stack = ColumnParallelStack(blocks, peers=g, gather="ce" if args.gather == "ce" else "peer")
+    ex = None
+    if args.activations == "int8":
+        ex = ActivationExchange(m, 4 * hid)
+        stack = ColumnParallelStack(blocks, peers=g, activations="int8", codes=ex)
+    else:
+        stack = ColumnParallelStack(blocks, peers=g, gather="ce" if args.gather == "ce" else "peer")
     del blocks
     torch.cuda.empty_cache()
 
@@ -945,12 +954,21 @@ def run_c5_multi(args, rank, world, local_rank):
     if world > 1:
         ms = _max_over_ranks(torch, dist, dev, ms)
     status = nat.device_status()
+    if ex is not None:
+        ex.close()
     g.close()
     if rank != 0:
         return
     flops = 2.0 * m * sum(n_ * k_ for n_, k_ in shapes) * nblocks
     recv = (world - 1) / world * m * sum(n_ for n_, _ in shapes) * 2 * nblocks
-    if args.gather == "ce":
+    if args.activations == "int8":
+        # the next layer's input columns as int8 (Q third, h, 4h, h per block; the last layer's fp16 output)
+        # plus the per-row absmax slots
+        cols = (hid + hid + 4 * hid + hid) * nblocks - hid
+        recv = (world - 1) / world * m * cols + (world - 1) / world * m * hid * 2 \
+            + (world - 1) * m * 4 * (4 * nblocks - 1)
+        stack_launches = 1 + 5 * (4 * nblocks - 1) + 2
+    elif args.gather == "ce":
         rows = -(-(-(-m // ce_chunks(world))) // 256) * 256
         stack_launches = 4 * nblocks * (2 * -(-m // rows) + (world - 1 if world > 1 else 0) + 1)
     else:
@@ -962,15 +980,19 @@ def run_c5_multi(args, rank, world, local_rank):
             "config": {"M": m, "hidden": hid, "blocks": nblocks,
                        "linears": "QKV 9216x3072, out 3072x3072 (on the Q third), up 12288x3072, down 3072x12288, "
                                   "block-128 rotation, every weight N-sharded over the ranks",
-                       "parallelism": f"column-parallel x{world}, every layer output gathered to every rank "
-                                      + ("by copy engines overlapping a chunked GEMM" if args.gather == "ce"
-                                         else "inside the GEMM epilogue (NVLink peer stores)")},
+                       "parallelism": f"column-parallel x{world}, " + (
+                           "only the next layer's input exchanged, as INT8 codes (slice rotation + per-row absmax "
+                           "exchange + quantize into every rank's code buffer); the last output gathered in fp16"
+                           if args.activations == "int8" else
+                           "every layer output gathered to every rank "
+                           + ("by copy engines overlapping a chunked GEMM" if args.gather == "ce"
+                              else "inside the GEMM epilogue (NVLink peer stores)"))},
             "roofline": {"bound": "nvlink", "nvlink_bytes_received_per_rank": int(recv),
                          "link_floor_ms": round(recv / 770e9 * 1e3, 3),
                          "gemm_floor_ms": round(flops / world / (2.0 * peaks()["bf16_tflops"] * 1e12) * 1e3, 3),
                          "frac": round(max(recv / 770e9 * 1e3,
                                            flops / world / (2.0 * peaks()["bf16_tflops"] * 1e12) * 1e3) / ms, 4)},
-            "gpu_launches": stack_launches * steps, "gather": args.gather,
+            "gpu_launches": stack_launches * steps, "gather": args.gather, "activations": args.activations,
             "gather_store": args.gather_store if args.gather != "ce" else None, "clocks": clocks.summary(),
             "device_status": status,
             "timing": "eager public ColumnParallelStack calls"}

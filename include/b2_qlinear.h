@@ -81,7 +81,7 @@ int b2_set_prologue_path(int path);
 int b2_set_w4a16_path(int path);
 
 /* Process-wide transport of the fused column-parallel gather
- * (b2_quant_linear_gather): 0 = default (1), 1 = each staged 32-row output
+ * (b2_quant_linear_gather): 0 = default (2), 1 = each staged 32-row output
  * unit copied to every peer by 16-byte SM stores from the epilogue warps,
  * 2 = by TMA stores through one tensor map per peer output.  Outputs,
  * flags and completion rules are identical for every choice.  No reference
@@ -298,6 +298,37 @@ int b2_quant_linear_gather_ce(int kind, const void* x, int x_dtype, int64_t M, i
                               void* workspace, size_t workspace_bytes, void* stream);
 int b2_gather_wait_ce(void* state, int world, int rank, void* stream);
 
+/* Column-parallel INT8 activation exchange for stacks of column-parallel
+ * linears (each layer's next layer reads whole rows of its output).  Rank
+ * `rank` of `world` holds a column slice y [M, Ns] (16-byte aligned rows of
+ * fp16/bf16/fp32, row stride ldy; Ns % 64 == 0, Ns <= 24576, Ns % block == 0,
+ * Ns may be 0) of the layer output; block is the next layer's rotation
+ * block (0/1 none, else a power of two <= 2048).
+ *
+ * Phase 1, b2_shard_amax: rotates the slice's blocks exactly as the
+ * activation prologue does, reduces each row to the absmax of its rotated
+ * values and stores it into slot [rank * M + row] of every rank's exchange
+ * buffer xchg[q] (fp32 [world][M]); then releases `epoch` into slot `rank`
+ * of every rank's state states[q] (b2_gather_state_bytes, 256-byte aligned).
+ * Phase 2, b2_shard_codes, after b2_gather_wait(phase-1 state, epoch): the
+ * row scale is max over the world slots of this rank's exchange buffer
+ * (= the whole row's absmax; max is exact) / 127 (int8, quant 0) or / 448
+ * (e4m3, quant 1); the slice's codes are written into columns [col0, col0 +
+ * Ns) of every rank's code buffer q_outs[q] (row stride ldq bytes, ldq % 16
+ * == 0, col0 % 16 == 0) and the scales into this rank's scale[M]; then
+ * `epoch` is released into slot `rank` of every rank's (phase-2) state.
+ * After b2_gather_wait on the phase-2 state every rank holds the codes and
+ * scales that b2_act_quant computes on the whole row, bit for bit.  Each
+ * phase needs its own state (epochs increase per state).  M == 0 launches
+ * nothing and releases nothing.  No reference counterpart: the reference is
+ * single-GPU; this is the multi-GPU form of its per-layer activation
+ * quantization (production/MOSS_RDNA2_INT8/backend.py:112-127). */
+int b2_shard_amax(const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block, int world,
+                  int rank, void* const* xchg, void* const* states, uint32_t epoch, void* stream);
+int b2_shard_codes(const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block, int quant,
+                   int world, int rank, const void* xchg_local, void* const* q_outs, int64_t ldq, int64_t col0,
+                   float* scale, void* const* states, uint32_t epoch, void* stream);
+
 /* Copy-engine copy of `rows` rows of `width_bytes` bytes between two device
  * buffers that may live on different GPUs (an IPC-mapped peer pointer, for
  * instance): the copy-engine counterpart of the gather, used to measure the
@@ -310,6 +341,18 @@ int b2_peer_copy_2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, 
  * that call has landed in the local output buffer.  Bounded: after 2 s the
  * kernel gives up and sets b2_device_status to 0x107. */
 int b2_gather_wait(const void* state, int world, uint32_t epoch, void* stream);
+
+/* The gathered GEMM on operands already quantized (b2_qgemm's arguments:
+ * codes a [M,K] with per-row a_scale, w [N,K] with w_scale; kind 0 INT8 or
+ * 1 e4m3) with b2_quant_linear_gather's output contract: this rank's N
+ * columns land at col0 of every rank's outs[q] and `epoch` is released into
+ * slot `rank` of every rank's states[q]; wait with b2_gather_wait.  For
+ * stacks whose layer inputs arrive as codes (b2_shard_codes).  No reference
+ * counterpart (the reference is single-GPU). */
+int b2_qgemm_gather(int kind, const void* a, int64_t lda, const float* a_scale, const void* w, int64_t ldw,
+                    int64_t M, int64_t N, int64_t K, const float* w_scale, int64_t w_scale_count, const void* bias,
+                    int bias_dtype, int epilogue, int out_dtype, int64_t ldc, int64_t col0, int world, int rank,
+                    void* const* outs, void* const* states, uint32_t epoch, void* stream);
 
 /* Allocation-free fused quantized linear: the same computation and results
  * as b2_quant_linear, for callers that cannot provide a workspace (a host

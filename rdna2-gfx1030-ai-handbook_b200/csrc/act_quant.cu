@@ -315,6 +315,45 @@ __global__ void __launch_bounds__(128)
 // (about 128 threads, at most kLaneThreads), several CTAs per SM.
 constexpr int kLaneE = 64;
 constexpr int kLaneThreads = 384;
+constexpr int kLaneFull = 0;
+constexpr int kLaneAmax = 1;
+constexpr int kLaneCodes = 2;
+
+// End of a sharded-mode launch, run by every thread: orders this thread's
+// peer stores, counts the CTA, and the last CTA releases the epoch into slot
+// `rank` of every rank's flag array and rearms the counter.
+__device__ __forceinline__ void shard_signal(const ShardArgs& sh) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t prev = atomicAdd(sh.done_count, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int r = 0; r < sh.world; ++r) st_release_sys(sh.flag_slot[r], sh.epoch);
+      *sh.done_count = 0u;
+    }
+  }
+}
+
+// A sharded launch whose slice is empty (this rank holds none of the next
+// layer's input columns): kLaneAmax writes 0 into its slots (the absmax of
+// nothing; 0 never raises a maximum of absolute values), kLaneCodes only
+// computes the row scales from the exchanged maxima.
+template <bool FP8>
+__global__ void shard_empty_kernel(int mode, int M, float* __restrict__ scale, const ShardArgs sh) {
+  for (int row = blockIdx.x * blockDim.x + threadIdx.x; row < M; row += gridDim.x * blockDim.x) {
+    if (mode == kLaneAmax) {
+      for (int r = 0; r < sh.world; ++r) sh.xchg[r][static_cast<int64_t>(sh.rank) * M + row] = 0.0f;
+    } else {
+      float amax = 0.0f;
+      for (int r = 0; r < sh.world; ++r) amax = fmaxf(amax, sh.xlocal[static_cast<int64_t>(r) * M + row]);
+      float sc = __fdiv_rn(amax, FP8 ? 448.0f : 127.0f);
+      if (!(sc > 0.0f)) sc = 1.0f;
+      scale[row] = sc;
+    }
+  }
+  shard_signal(sh);
+}
 
 template <int DT, int E>
 __device__ __forceinline__ void load_slice(const void* x, int64_t off, bool live, float (&v)[E]) {
@@ -357,12 +396,29 @@ __device__ __forceinline__ uint32_t code_markstein(float v, float s, float r) {
   return __float_as_uint(__fadd_rn(z, 12582912.0f));  // low byte = rint(z), |z| <= 127
 }
 
-template <int DT, bool FP8 = false, int E = kLaneE>
+// Modes of the lane kernel.  kLaneFull: codes and scales of whole rows.
+// The two sharded modes serve a column-parallel layer whose next layer reads
+// the whole row: each rank holds a column slice of the row (whole rotation
+// blocks), kLaneAmax writes the slice's absmax of the rotated values into
+// slot `rank` of every rank's exchange buffer [world][M]; kLaneCodes takes
+// the row's absmax as the maximum over the world slots (exactly the whole
+// row's absmax: max is exact), and writes the slice's codes into the same
+// columns of every rank's code buffer and the row scale locally.  Codes and
+// scales are bit-identical to kLaneFull on the whole row.  Both sharded
+// modes end with the gather signal: a system-scope fence, a CTA count, and
+// the last CTA releasing `epoch` into slot `rank` of every rank's flags.
+
+template <int DT, bool FP8 = false, int E = kLaneE, int MODE = kLaneFull>
 __global__ void __launch_bounds__(kLaneThreads, 1)
     act_quant_lane_kernel(const void* __restrict__ x, int64_t ldx, int M, int K, int tpr, int rows_per_cta,
                           int block, float inv, uint8_t* __restrict__ q, int64_t ldq, float* __restrict__ scale,
-                          int early) {
+                          int early, const ShardArgs sh) {
   __shared__ uint32_t s_max[3][kLaneThreads];
+  // kLaneCodes: the CTA's codes are staged in shared memory (two buffers of
+  // rows_per_cta x K bytes) and each row leaves as one bulk store per rank,
+  // issued by the row's first lane after the next CTA barrier, so that the
+  // stores to the peers stream while the next rows are rotated.
+  extern __shared__ __align__(128) uint8_t s_stage[];
   if (early) griddep_launch_dependents();  // the GEMM may set up while the codes are written
   const int tid = threadIdx.x;
   const int r_local = tid / tpr;
@@ -370,6 +426,12 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
   const bool active = r_local < rows_per_cta;
   const int lane = tid & 31;
   const int64_t row_step = static_cast<int64_t>(gridDim.x) * rows_per_cta;
+  int64_t staged_row = -1;  // kLaneCodes, first lane of a row: the row staged in the previous iteration
+  auto send_row = [&](int buf) {
+    const uint32_t src = smem_u32(s_stage) + static_cast<uint32_t>((buf * rows_per_cta + r_local) * K);
+    for (int r = 0; r < sh.world; ++r) bulk_store(sh.qout[r] + staged_row * ldq, src, static_cast<uint32_t>(K));
+    bulk_commit_group();
+  };
   for (int i = tid; i < 3 * kLaneThreads; i += blockDim.x) (&s_max[0][0])[i] = 0u;
   // 16-bit rows with E = 64: the next row group's slice (32 registers) is in
   // flight while the current one is rotated and quantized.
@@ -460,13 +522,39 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
     const int sb = it % 3;
     if (live) atomicMax(&s_max[sb][r_local], __float_as_uint(amax));
     for (int i = tid; i < rows_per_cta; i += blockDim.x) s_max[(it + 1) % 3][i] = 0u;  // next iteration's
+    if constexpr (MODE == kLaneCodes) {
+      if (part == 0 && active) bulk_wait_read<0>();  // this iteration's buffer is free again
+    }
     __syncthreads();
+    if constexpr (MODE == kLaneCodes) {
+      if (part == 0 && active) {
+        if (staged_row >= 0) send_row((it + 1) & 1);
+        staged_row = live ? row : -1;
+      }
+    }
     if (!live) continue;
     amax = __uint_as_float(s_max[sb][r_local]);
+    if constexpr (MODE == kLaneAmax) {
+      if (part == 0)
+        for (int r = 0; r < sh.world; ++r) sh.xchg[r][static_cast<int64_t>(sh.rank) * M + row] = amax;
+      continue;
+    }
+    if constexpr (MODE == kLaneCodes) {
+      amax = 0.0f;
+      for (int r = 0; r < sh.world; ++r) amax = fmaxf(amax, sh.xlocal[static_cast<int64_t>(r) * M + row]);
+    }
     float sc = __fdiv_rn(amax, FP8 ? 448.0f : 127.0f);
     if (!(sc > 0.0f)) sc = 1.0f;
 
     uint8_t* dst = q + row * ldq + static_cast<int64_t>(part) * E;
+    uint8_t* stage = s_stage + ((it & 1) * rows_per_cta + r_local) * K + part * E;
+    auto put = [&](int j, const uint4& v) {
+      if constexpr (MODE == kLaneCodes) {
+        *reinterpret_cast<uint4*>(stage + 16 * j) = v;
+      } else {
+        *reinterpret_cast<uint4*>(dst + 16 * j) = v;
+      }
+    };
     // Normal, finite scales: |RN(v/s)| <= 127 with no clamp needed, since
     // s = RN(absmax/127) carries a relative error below 2^-24.  Subnormal
     // scales lose that precision (quotients can exceed 127.5) and take the
@@ -525,7 +613,7 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
             o[t2] = __byte_perm(__byte_perm(c0, c1, 0x0040), __byte_perm(c2, c3, 0x0040), 0x5410);
           }
         }
-        *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(o[0], o[1], o[2], o[3]);
+        put(j, make_uint4(o[0], o[1], o[2], o[3]));
       }
     } else {
 #pragma unroll
@@ -542,11 +630,21 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
                                 __byte_perm(slow_int8(p1.x, sc), slow_int8(p1.y, sc), 0x0040), 0x5410);
           }
         }
-        *reinterpret_cast<uint4*>(dst + 16 * j) = make_uint4(o[0], o[1], o[2], o[3]);
+        put(j, make_uint4(o[0], o[1], o[2], o[3]));
       }
     }
     if (part == 0) scale[row] = sc;
+    if constexpr (MODE == kLaneCodes) fence_proxy_async_smem();  // staged codes visible to the bulk stores
   }
+  if constexpr (MODE == kLaneCodes) {
+    __syncthreads();
+    if (part == 0 && active) {
+      if (staged_row >= 0) send_row((it + 1) & 1);
+      bulk_wait_all();               // every row at every rank
+      fence_proxy_async_global();
+    }
+  }
+  if constexpr (MODE != kLaneFull) shard_signal(sh);
 }
 
 // 0 automatic (the lane-block kernel where it applies, else the warp-shuffle
@@ -558,14 +656,27 @@ void set_prologue_path(int path) { g_prologue_path = path; }
 // Small CTAs (about 128 threads: whole rows of TPR lanes), several per SM,
 // so that one CTA's loads overlap another's arithmetic across the per-row
 // barrier.
-template <int DT, bool FP8>
+template <int DT, bool FP8, int MODE = kLaneFull>
 static cudaError_t launch_lane(int64_t M, cudaStream_t st, const void* x, int64_t ldx, int K, int block,
-                               float inv, uint8_t* q, int64_t ldq, float* scale, int early) {
-  auto kernel = act_quant_lane_kernel<DT, FP8>;
+                               float inv, uint8_t* q, int64_t ldq, float* scale, int early,
+                               const ShardArgs& sh = ShardArgs{}) {
+  auto kernel = act_quant_lane_kernel<DT, FP8, kLaneE, MODE>;
   const int tpr = K / kLaneE;
   int rows = 128 / tpr;
   if (rows < 1) rows = 1;
   const int threads = (rows * tpr + 31) / 32 * 32;
+  // kLaneCodes stages two buffers of rows x K code bytes (at most 48 KiB)
+  const size_t dyn = MODE == kLaneCodes ? static_cast<size_t>(2 * rows * K) : 0;
+  if (MODE == kLaneCodes) {
+    static bool configured[64] = {false};
+    int d = 0;
+    cudaGetDevice(&d);
+    if (d < 64 && !configured[d]) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 384 * kLaneE);
+      if (e != cudaSuccess) return e;
+      configured[d] = true;
+    }
+  }
   static int per_sm[64][8] = {{0}};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -574,13 +685,14 @@ static cudaError_t launch_lane(int64_t M, cudaStream_t st, const void* x, int64_
   if (dev < 64 && slot < 8 && per_sm[dev][slot] > 0) {
     n = per_sm[dev][slot];
   } else {
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess || n <= 0) n = 1;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, dyn) != cudaSuccess || n <= 0) n = 1;
     if (dev < 64 && slot < 8) per_sm[dev][slot] = n;
   }
   const int64_t need = (M + rows - 1) / rows;
   const int64_t cap = static_cast<int64_t>(device_sm_count()) * n;
   const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
-  kernel<<<grid, threads, 0, st>>>(x, ldx, static_cast<int>(M), K, tpr, rows, block, inv, q, ldq, scale, early);
+  kernel<<<grid, threads, dyn, st>>>(x, ldx, static_cast<int>(M), K, tpr, rows, block, inv, q, ldq, scale, early,
+                                     sh);
   return cudaGetLastError();
 }
 
@@ -699,6 +811,38 @@ cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int6
   B2_AQ_DT(2)
 #undef B2_AQ_DT
 #undef B2_AQ
+}
+
+cudaError_t run_shard_quant(int mode, const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block,
+                            int quant, int64_t ldq, float* scale, const ShardArgs& sh, cudaStream_t stream) {
+  if (M <= 0) return cudaSuccess;
+  if (mode != kLaneAmax && mode != kLaneCodes) return cudaErrorInvalidValue;
+  if (Ns == 0) {
+    const int64_t blocks = (M + 255) / 256;
+    const unsigned grid = static_cast<unsigned>(blocks < 1024 ? blocks : 1024);
+    if (quant == 1)
+      shard_empty_kernel<true><<<grid, 256, 0, stream>>>(mode, static_cast<int>(M), scale, sh);
+    else
+      shard_empty_kernel<false><<<grid, 256, 0, stream>>>(mode, static_cast<int>(M), scale, sh);
+    return cudaGetLastError();
+  }
+  const float inv = block > 1 ? static_cast<float>(1.0 / sqrt(static_cast<double>(block))) : 1.0f;
+  const int k = static_cast<int>(Ns);
+#define B2_SQ(DT, F)                                                                                        \
+  return mode == kLaneAmax                                                                                  \
+             ? launch_lane<DT, F, kLaneAmax>(M, stream, y, ldy, k, block, inv, nullptr, ldq, scale, 0, sh)  \
+             : launch_lane<DT, F, kLaneCodes>(M, stream, y, ldy, k, block, inv, nullptr, ldq, scale, 0, sh)
+#define B2_SQ_DT(F)                  \
+  switch (y_dtype) {                 \
+    case kF32: B2_SQ(kF32, F);       \
+    case kF16: B2_SQ(kF16, F);       \
+    case kBF16: B2_SQ(kBF16, F);     \
+    default: return cudaErrorInvalidValue; \
+  }
+  if (quant == 1) { B2_SQ_DT(true) }
+  B2_SQ_DT(false)
+#undef B2_SQ_DT
+#undef B2_SQ
 }
 
 // fp8 (e4m3fn / e5m2) -> fp32 / fp16 decode, exact for every finite pattern;

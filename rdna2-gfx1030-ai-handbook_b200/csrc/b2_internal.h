@@ -13,7 +13,23 @@ constexpr int kMaxGatherPeers = 7;
 // maps (kGatherTma).
 constexpr int kGatherSm = 1;
 constexpr int kGatherTma = 2;
-constexpr int kGatherDefault = kGatherSm;
+constexpr int kGatherDefault = kGatherTma;
+
+// Arguments of the sharded activation-prologue modes (column-parallel layers
+// whose next layer reads whole rows): exchange buffers [world][M] fp32 of
+// every rank (amax mode) or this rank's (codes mode), every rank's code
+// buffer at this rank's first column (codes mode), and the completion
+// signal: slot `rank` of every rank's flag array, this rank's CTA counter.
+struct ShardArgs {
+  int world = 0;
+  int rank = 0;
+  float* xchg[kMaxGatherPeers + 1] = {};
+  const float* xlocal = nullptr;
+  uint8_t* qout[kMaxGatherPeers + 1] = {};
+  uint32_t* flag_slot[kMaxGatherPeers + 1] = {};
+  uint32_t* done_count = nullptr;
+  uint32_t epoch = 0;
+};
 
 struct GemmParams {
   int M, N, K;
@@ -51,6 +67,12 @@ struct GemmParams {
   uint32_t epoch;
 };
 
+// Argument check of the GEMM on quantized operands (b2_qgemm): 0 when
+// valid, including every M == 0 or N == 0 call.
+int check_gemm_args(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N,
+                    int64_t K, const float* a_scale, const float* b_scale, int64_t b_scale_count,
+                    const void* bias, int bias_dtype, int epilogue, const void* out, int out_dtype, int64_t ldc);
+
 // Argument check of the fused linear (b2_quant_linear): 0 when valid,
 // including every M == 0 or N == 0 call; the gather variant shares it.
 int check_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
@@ -81,6 +103,11 @@ int pair_capacity();
 // GEMM, launched with programmatic serialization) start its setup and
 // weight loads while this one runs; only for callers whose next kernel reads
 // nothing else this kernel's predecessors may still write.
+// One sharded prologue launch (mode 1 = amax exchange, 2 = codes) over a
+// column slice [M, Ns] of 16/32-bit activations; Ns may be 0.
+cudaError_t run_shard_quant(int mode, const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block,
+                            int quant, int64_t ldq, float* scale, const ShardArgs& sh, cudaStream_t stream);
+
 cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx,
                           int block, int quant, void* q, int64_t ldq, float* scale,
                           cudaStream_t stream, bool early_dependents = false);

@@ -147,6 +147,14 @@ size_t b2_quant_linear_workspace_bytes(int64_t M, int64_t K) {
 
 }  // extern "C"
 
+int b2::check_gemm_args(int kind, const void* a, int64_t lda, const void* b, int64_t ldb, int64_t M, int64_t N,
+                        int64_t K, const float* a_scale, const float* b_scale, int64_t b_scale_count,
+                        const void* bias, int bias_dtype, int epilogue, const void* out, int out_dtype,
+                        int64_t ldc) {
+  return check_gemm(kind, a, lda, b, ldb, M, N, K, a_scale, b_scale, b_scale_count, bias, bias_dtype, epilogue,
+                    out, out_dtype, ldc);
+}
+
 // Argument check of the fused linear (shared with the gather variant):
 // 0 when the call is valid, including every M == 0 or N == 0 call.
 int b2::check_quant_linear(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,

@@ -147,11 +147,14 @@ int b2_gather_wait(const void* state, int world, uint32_t epoch, void* stream) {
   return static_cast<int>(cudaGetLastError());
 }
 
-int b2_quant_linear_gather(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
-                           const void* w, int64_t ldw, int64_t N, const float* w_scale, int64_t w_scale_count,
-                           const void* bias, int bias_dtype, int epilogue, int out_dtype, int64_t ldc,
-                           int64_t col0, int world, int rank, void* const* outs, void* const* states,
-                           uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Gather arguments shared by the two gathered GEMM entry points: 0 when the
+// output buffers, states and column range are valid.
+int check_gather(int world, int rank, int64_t N, int64_t ldc, int64_t col0, int out_dtype, void* const* outs,
+                 void* const* states, uint32_t epoch) {
   if (world < 1 || world > b2::kMaxGatherPeers + 1 || rank < 0 || rank >= world) return fail();
   if (!outs || !states || epoch == 0) return fail();
   if (out_dtype != b2::kF16 && out_dtype != b2::kBF16 && out_dtype != b2::kF32) return fail();
@@ -161,6 +164,72 @@ int b2_quant_linear_gather(int kind, const void* x, int x_dtype, int64_t M, int6
     if (!outs[q] || !aligned16(outs[q]) || !states[q]) return fail();
     if (reinterpret_cast<uintptr_t>(states[q]) % 256 != 0) return fail();
   }
+  return 0;
+}
+
+// Peer outputs (this rank's columns of every other rank's buffer), flag
+// slots (peers first, own last), the CTA counter and the epoch.
+void fill_gather(b2::GemmParams& p, int world, int rank, int64_t col0, int ob, void* const* outs,
+                 void* const* states, uint32_t epoch) {
+  p.vec_ok = 1;
+  p.gather = 1;
+  p.n_peers = 0;
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    p.peer_out[p.n_peers++] = static_cast<char*>(outs[r]) + col0 * ob;
+  }
+  int slot = 0;
+  for (int r = 0; r < world; ++r) {
+    if (r == rank) continue;
+    p.flag_slot[slot++] = static_cast<uint32_t*>(states[r]) + rank;
+  }
+  p.flag_slot[slot] = static_cast<uint32_t*>(states[rank]) + rank;
+  p.done_count = reinterpret_cast<uint32_t*>(static_cast<char*>(states[rank]) + kCounterOffset);
+  p.epoch = epoch;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2_qgemm_gather(int kind, const void* a, int64_t lda, const float* a_scale, const void* w, int64_t ldw,
+                    int64_t M, int64_t N, int64_t K, const float* w_scale, int64_t w_scale_count, const void* bias,
+                    int bias_dtype, int epilogue, int out_dtype, int64_t ldc, int64_t col0, int world, int rank,
+                    void* const* outs, void* const* states, uint32_t epoch, void* stream) {
+  if (kind != b2::kKindI8 && kind != b2::kKindE4M3) return fail();
+  int st = check_gather(world, rank, N, ldc, col0, out_dtype, outs, states, epoch);
+  if (st != 0) return st;
+  const int ob = out_dtype == b2::kF32 ? 4 : 2;
+  char* own = static_cast<char*>(outs[rank]) + col0 * ob;
+  st = b2::check_gemm_args(kind, a, lda, w, ldw, M, N, K, a_scale, w_scale, w_scale_count, bias, bias_dtype,
+                           epilogue, own, out_dtype, ldc);
+  if (st != 0 || M == 0) return st;
+  if (epilogue == b2::kEpiNone) return fail();
+  b2::GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.sa = a_scale;
+  p.sb = w_scale;
+  p.sb_scalar = w_scale_count == 1 ? 1 : 0;
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.out = own;
+  p.out_dtype = out_dtype;
+  p.ldc = ldc;
+  p.epilogue = epilogue;
+  fill_gather(p, world, rank, col0, ob, outs, states, epoch);
+  return static_cast<int>(b2::run_qgemm(kind, a, lda, w, ldw, p, 0, static_cast<cudaStream_t>(stream)));
+}
+
+int b2_quant_linear_gather(int kind, const void* x, int x_dtype, int64_t M, int64_t K, int64_t ldx, int block,
+                           const void* w, int64_t ldw, int64_t N, const float* w_scale, int64_t w_scale_count,
+                           const void* bias, int bias_dtype, int epilogue, int out_dtype, int64_t ldc,
+                           int64_t col0, int world, int rank, void* const* outs, void* const* states,
+                           uint32_t epoch, void* workspace, size_t workspace_bytes, void* stream) {
+  int st0 = check_gather(world, rank, N, ldc, col0, out_dtype, outs, states, epoch);
+  if (st0 != 0) return st0;
+  const int ob = out_dtype == b2::kF32 ? 4 : 2;
   char* own = static_cast<char*>(outs[rank]) + col0 * ob;
   // The fused linear's own argument check, with this rank's columns of its
   // own output as `out`.  M == 0 launches nothing and releases no flag, so
@@ -188,22 +257,8 @@ int b2_quant_linear_gather(int kind, const void* x, int x_dtype, int64_t M, int6
   p.out_dtype = out_dtype;
   p.ldc = ldc;
   p.epilogue = epilogue;
-  p.vec_ok = 1;
   p.weight_prefetch = 1;
-  p.gather = 1;
-  p.n_peers = 0;
-  for (int r = 0; r < world; ++r) {
-    if (r == rank) continue;
-    p.peer_out[p.n_peers++] = static_cast<char*>(outs[r]) + col0 * ob;
-  }
-  int slot = 0;
-  for (int r = 0; r < world; ++r) {
-    if (r == rank) continue;
-    p.flag_slot[slot++] = static_cast<uint32_t*>(states[r]) + rank;
-  }
-  p.flag_slot[slot] = static_cast<uint32_t*>(states[rank]) + rank;
-  p.done_count = reinterpret_cast<uint32_t*>(static_cast<char*>(states[rank]) + kCounterOffset);
-  p.epoch = epoch;
+  fill_gather(p, world, rank, col0, ob, outs, states, epoch);
   return static_cast<int>(b2::run_qgemm(kind, q, ldq, w, ldw, p, 0, s));
 }
 
@@ -368,4 +423,75 @@ extern "C" int b2_gather_wait_ce(void* state, int world, int rank, void* stream)
   ce_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint32_t*>(state), world, rank,
                                                                   b2::status_word_ptr());
   return static_cast<int>(cudaGetLastError());
+}
+
+// ------------------------------------ column-parallel INT8 activation exchange
+// For a stack of column-parallel layers, the next layer's input is gathered
+// as INT8 codes instead of fp16 outputs (half the bytes): each rank rotates
+// and reduces its own column slice of the layer output (whole rotation
+// blocks), the per-row absmax slices are exchanged (b2_shard_amax), and each
+// rank quantizes its slice with the row's global scale straight into every
+// rank's code buffer (b2_shard_codes).  Each phase ends by releasing `epoch`
+// into slot `rank` of every rank's state; b2_gather_wait on the local state
+// (one per phase) is the barrier before the next phase / the next GEMM.
+namespace {
+
+int shard_checks(const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block, int world, int rank,
+                 void* const* states, uint32_t epoch) {
+  if (world < 1 || world > b2::kMaxGatherPeers + 1 || rank < 0 || rank >= world) return fail();
+  if (!states || epoch == 0 || M < 0 || M > INT32_MAX || Ns < 0 || Ns % 64 != 0 || Ns / 64 > 384) return fail();
+  if (y_dtype != b2::kF16 && y_dtype != b2::kBF16 && y_dtype != b2::kF32) return fail();
+  if (block > 1 && ((block & (block - 1)) != 0 || block > 2048 || (Ns > 0 && Ns % block != 0))) return fail();
+  if (block < 0) return fail();
+  const int eb = y_dtype == b2::kF32 ? 4 : 2;
+  if (Ns > 0 && M > 0 && (!y || !aligned16(y) || ldy < Ns || (ldy * eb) % 16 != 0)) return fail();
+  for (int q = 0; q < world; ++q)
+    if (!states[q] || reinterpret_cast<uintptr_t>(states[q]) % 256 != 0) return fail();
+  return 0;
+}
+
+void shard_signal_args(b2::ShardArgs& sh, int world, int rank, void* const* states, uint32_t epoch) {
+  sh.world = world;
+  sh.rank = rank;
+  for (int q = 0; q < world; ++q) sh.flag_slot[q] = static_cast<uint32_t*>(states[q]) + rank;
+  sh.done_count = reinterpret_cast<uint32_t*>(static_cast<char*>(states[rank]) + kCounterOffset);
+  sh.epoch = epoch;
+}
+
+}  // namespace
+
+extern "C" int b2_shard_amax(const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block, int world,
+                             int rank, void* const* xchg, void* const* states, uint32_t epoch, void* stream) {
+  int st = shard_checks(y, y_dtype, M, Ns, ldy, block, world, rank, states, epoch);
+  if (st != 0) return st;
+  if (!xchg) return fail();
+  for (int q = 0; q < world; ++q)
+    if (!xchg[q] || reinterpret_cast<uintptr_t>(xchg[q]) % 4 != 0) return fail();
+  if (M == 0) return 0;
+  b2::ShardArgs sh;
+  shard_signal_args(sh, world, rank, states, epoch);
+  for (int q = 0; q < world; ++q) sh.xchg[q] = static_cast<float*>(xchg[q]);
+  return static_cast<int>(b2::run_shard_quant(1, y, y_dtype, M, Ns, ldy, block, 0, 0, nullptr, sh,
+                                              static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" int b2_shard_codes(const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block, int quant,
+                              int world, int rank, const void* xchg_local, void* const* q_outs, int64_t ldq,
+                              int64_t col0, float* scale, void* const* states, uint32_t epoch, void* stream) {
+  int st = shard_checks(y, y_dtype, M, Ns, ldy, block, world, rank, states, epoch);
+  if (st != 0) return st;
+  if (quant != 0 && quant != 1) return fail();
+  if (!xchg_local || reinterpret_cast<uintptr_t>(xchg_local) % 4 != 0 || !q_outs || !scale) return fail();
+  if (reinterpret_cast<uintptr_t>(scale) % 4 != 0 || col0 < 0 || ldq % 16 != 0 || col0 % 16 != 0 ||
+      col0 + Ns > ldq)
+    return fail();
+  for (int q = 0; q < world; ++q)
+    if (!q_outs[q] || !aligned16(q_outs[q])) return fail();
+  if (M == 0) return 0;
+  b2::ShardArgs sh;
+  shard_signal_args(sh, world, rank, states, epoch);
+  sh.xlocal = static_cast<const float*>(xchg_local);
+  for (int q = 0; q < world; ++q) sh.qout[q] = static_cast<uint8_t*>(q_outs[q]) + col0;
+  return static_cast<int>(b2::run_shard_quant(2, y, y_dtype, M, Ns, ldy, block, quant, ldq, scale, sh,
+                                              static_cast<cudaStream_t>(stream)));
 }

@@ -68,11 +68,17 @@ SIGNATURES = {
                                 _int, _int, _i64, _i64, _int, _int, ctypes.POINTER(_p), ctypes.POINTER(_p),
                                 ctypes.c_uint32, _p, _size, _p], _int),
     "b2_gather_wait": ([_p, _int, ctypes.c_uint32, _p], _int),
+    "b2_qgemm_gather": ([_int, _p, _i64, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p, _int, _int, _int, _i64,
+                         _i64, _int, _int, ctypes.POINTER(_p), ctypes.POINTER(_p), ctypes.c_uint32, _p], _int),
     "b2_peer_copy_2d": ([_p, _i64, _p, _i64, _i64, _i64, _p], _int),
     "b2_quant_linear_gather_ce": ([_int, _p, _int, _i64, _i64, _i64, _int, _p, _i64, _i64, _p, _i64, _p, _int,
                                    _int, _int, _i64, _i64, _int, _int, ctypes.POINTER(_p), ctypes.POINTER(_p),
                                    _int, _p, _size, _p], _int),
     "b2_gather_wait_ce": ([_p, _int, _int, _p], _int),
+    "b2_shard_amax": ([_p, _int, _i64, _i64, _i64, _int, _int, _int, ctypes.POINTER(_p), ctypes.POINTER(_p),
+                       ctypes.c_uint32, _p], _int),
+    "b2_shard_codes": ([_p, _int, _i64, _i64, _i64, _int, _int, _int, _int, _p, ctypes.POINTER(_p), _i64, _i64,
+                        _p, ctypes.POINTER(_p), ctypes.c_uint32, _p], _int),
     "b2_quant_linear_noalloc_max_bytes": ([], _size),
     "b2_quant_linear_noalloc": ([_int, _p, _int, _i64, _i64, _i64, _int, _p, _i64, _i64, _p, _i64,
                                  _p, _int, _int, _p, _int, _i64, _p], _int),

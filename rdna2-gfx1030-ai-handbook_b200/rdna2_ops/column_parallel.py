@@ -67,6 +67,45 @@ def ce_chunks(world):
     return 1 if world == 1 else 4 if world == 2 else 2 if world <= 4 else 1
 
 
+def _map_peers(lib, tensors, world, rank, group, exchange):
+    """Export every tensor's IPC handle, exchange the handles (one
+    all_gather_object, or `exchange` in tests) and map every peer's tensors.
+    Returns (per tensor, a ctypes array of the world ranks' device pointers
+    -- this rank's own tensor at index `rank`) and the imported handles."""
+    def export(t):
+        h = ctypes.create_string_buffer(lib.b2_ipc_handle_bytes())
+        off = ctypes.c_uint64(0)
+        nat.check(lib.b2_ipc_export(t.data_ptr(), h, ctypes.byref(off)), "b2_ipc_export")
+        return bytes(h.raw), int(off.value)
+
+    mine = [export(t) for t in tensors]
+    if exchange is not None:
+        everyone = exchange(mine)
+    elif world == 1:
+        everyone = [mine]
+    else:
+        everyone = [None] * world
+        dist.all_gather_object(everyone, mine, group=group)
+    imported = []
+    ptrs = [[None] * world for _ in tensors]
+    for r, entries in enumerate(everyone):
+        for i, (handle, offset) in enumerate(entries):
+            if r == rank:
+                ptrs[i][r] = tensors[i].data_ptr()
+                continue
+            ptr = ctypes.c_void_p()
+            nat.check(lib.b2_ipc_import(handle, offset, ctypes.byref(ptr)), "b2_ipc_import")
+            imported.append(handle)
+            ptrs[i][r] = ptr.value
+    arr = ctypes.c_void_p * world
+    return [arr(*p) for p in ptrs], imported
+
+
+def _unmap_peers(lib, imported):
+    while imported:
+        nat.check(lib.b2_ipc_release(imported.pop()), "b2_ipc_release")
+
+
 class PeerGather:
     """Output buffers shared by the ranks of a process group for the fused
     column-parallel gather.
@@ -96,36 +135,11 @@ class PeerGather:
         if self.state.data_ptr() % 256:
             raise RuntimeError("gather state must be 256-byte aligned")
         self.epoch = 0
-        self._imported = []
-        mine = [self._export(t) for t in self.local + [self.state]]
-        if exchange is not None:
-            everyone = exchange(mine)
-        elif self.world == 1:
-            everyone = [mine]
-        else:
-            everyone = [None] * self.world
-            dist.all_gather_object(everyone, mine, group=group)
-        ptrs = [[None] * self.world for _ in range(buffers + 1)]
-        for r, entries in enumerate(everyone):
-            for i, (handle, offset) in enumerate(entries):
-                ptrs[i][r] = (self.local + [self.state])[i].data_ptr() if r == self.rank \
-                    else self._import(handle, offset)
-        arr = ctypes.c_void_p * self.world
-        self.outs = [arr(*p) for p in ptrs[:buffers]]
-        self.states = arr(*ptrs[buffers])
+        arrays, self._imported = _map_peers(self.lib, self.local + [self.state], self.world, self.rank, group,
+                                            exchange)
+        self.outs = arrays[:buffers]
+        self.states = arrays[buffers]
         torch.cuda.synchronize(self.device)
-
-    def _export(self, t):
-        h = ctypes.create_string_buffer(self.lib.b2_ipc_handle_bytes())
-        off = ctypes.c_uint64(0)
-        nat.check(self.lib.b2_ipc_export(t.data_ptr(), h, ctypes.byref(off)), "b2_ipc_export")
-        return bytes(h.raw), int(off.value)
-
-    def _import(self, handle, offset):
-        ptr = ctypes.c_void_p()
-        nat.check(self.lib.b2_ipc_import(handle, offset, ctypes.byref(ptr)), "b2_ipc_import")
-        self._imported.append(handle)
-        return ptr.value
 
     def close(self, barrier=True):
         """Unmap the peers' buffers.  Collective by default: every rank calls
@@ -133,8 +147,7 @@ class PeerGather:
         has unmapped, so no rank frees buffers a peer still maps (a caller
         that synchronizes the ranks itself passes barrier=False)."""
         torch.cuda.synchronize(self.device)
-        while self._imported:
-            nat.check(self.lib.b2_ipc_release(self._imported.pop()), "b2_ipc_release")
+        _unmap_peers(self.lib, self._imported)
         if barrier and self.world > 1 and dist.is_initialized():
             dist.barrier(group=self.group)
 
@@ -145,6 +158,77 @@ class PeerGather:
 
     def wait(self, epoch, stream):
         nat.check(self.lib.b2_gather_wait(self.state.data_ptr(), self.world, epoch, stream), "b2_gather_wait")
+
+
+class ActivationExchange:
+    """Buffers of the column-parallel INT8 activation exchange (C ABI
+    b2_shard_amax / b2_shard_codes): per rank a per-row absmax exchange
+    buffer [world, m_max] fp32, two alternating code buffers [m_max,
+    round16(k_max)] int8 that the peers write into, the row scales [m_max]
+    (local) and one completion state per phase, all mapped by every peer
+    like PeerGather's buffers.  `close()` is collective like
+    PeerGather.close."""
+
+    def __init__(self, m_max, k_max, *, group=None, device=None, exchange=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.lib = nat.library()
+        self.m_max = int(m_max)
+        self.ldq = -(-int(k_max) // 16) * 16
+        sb = self.lib.b2_gather_state_bytes()
+        self.xchg = torch.zeros(self.world * self.m_max, device=self.device, dtype=torch.float32)
+        self.codes = [torch.empty((self.m_max, self.ldq), device=self.device, dtype=torch.int8) for _ in range(2)]
+        self.scale = torch.empty(self.m_max, device=self.device, dtype=torch.float32)
+        self.state_amax = torch.zeros(sb, device=self.device, dtype=torch.uint8)
+        self.state_codes = torch.zeros(sb, device=self.device, dtype=torch.uint8)
+        for st in (self.state_amax, self.state_codes):
+            if st.data_ptr() % 256:
+                raise RuntimeError("exchange state must be 256-byte aligned")
+        arrays, self._imported = _map_peers(
+            self.lib, [self.xchg] + self.codes + [self.state_amax, self.state_codes], self.world, self.rank, group,
+            exchange)
+        self.xchg_ptrs = arrays[0]
+        self.code_ptrs = arrays[1:3]
+        self.amax_states, self.code_states = arrays[3], arrays[4]
+        self.epoch_amax = 0
+        self.epoch_codes = 0
+        torch.cuda.synchronize(self.device)
+
+    def close(self, barrier=True):
+        torch.cuda.synchronize(self.device)
+        _unmap_peers(self.lib, self._imported)
+        if barrier and self.world > 1 and dist.is_initialized():
+            dist.barrier(group=self.group)
+
+    def exchange_slice(self, y, m, width, ldy, block, dst, col0, stream):
+        """Every rank's codes and this rank's scales for the next layer from
+        this rank's slice y [m, width] (row stride ldy) of the layer output:
+        the two phases and their waits, enqueued on `stream`.  `dst` selects
+        the code buffer, `col0` the slice's first column in the next layer's
+        input."""
+        lib = self.lib
+        ptr = y if isinstance(y, int) else y.data_ptr()
+        self.epoch_amax += 1
+        nat.check(lib.b2_shard_amax(ptr, nat.F16, m, width, ldy, block, self.world, self.rank, self.xchg_ptrs,
+                                    self.amax_states, self.epoch_amax, stream), "b2_shard_amax")
+        nat.check(lib.b2_gather_wait(self.state_amax.data_ptr(), self.world, self.epoch_amax, stream),
+                  "b2_gather_wait")
+        self.epoch_codes += 1
+        nat.check(lib.b2_shard_codes(ptr, nat.F16, m, width, ldy, block, 0, self.world, self.rank,
+                                     self.xchg.data_ptr(), self.code_ptrs[dst], self.ldq, col0,
+                                     self.scale.data_ptr(), self.code_states, self.epoch_codes, stream),
+                  "b2_shard_codes")
+        nat.check(lib.b2_gather_wait(self.state_codes.data_ptr(), self.world, self.epoch_codes, stream),
+                  "b2_gather_wait")
+
+
+def shard_overlap(c0, width, lo, hi):
+    """This rank's part [a, b) of the next layer's input columns [lo, hi),
+    given its output columns [c0, c0 + width); (a, a) when they miss."""
+    a, b = max(c0, lo), min(c0 + width, hi)
+    return (a, b) if a < b else (max(lo, min(c0, hi)), max(lo, min(c0, hi)))
 
 
 class ColumnParallelLinear:
@@ -261,21 +345,110 @@ class ColumnParallelStack:
     """The linear chain of BASELINE config 5's DiT blocks, column-parallel:
     per block QKV [3h, h], the out projection on the Q third of the QKV
     output (read in place through its row stride), up [4h, h] and down
-    [h, 4h], every one a W8A8 fused linear with block rotation whose output is
-    reassembled on every rank before the next linear reads it.  (Attention is
-    not on this path.)  `blocks` holds, per block, four (w_q [N,K], w_scale)
-    pairs of the full quantized weights; each rank keeps only its shards.
-    With a PeerGather the gathers run inside the GEMM epilogues and the layer
-    outputs alternate between its two buffers."""
+    [h, 4h], every one a W8A8 fused linear with block rotation.  (Attention
+    is not on this path.)  `blocks` holds, per block, four (w_q [N,K],
+    w_scale) pairs of the full quantized weights; each rank keeps only its
+    shards.
+
+    activations="fp16": every layer output is reassembled on every rank
+    before the next linear reads it (with a PeerGather the gathers run
+    inside the GEMM epilogues).  activations="int8" (needs `codes`, an
+    ActivationExchange, and `peers`): only the next layer's input travels,
+    as INT8 codes -- each rank rotates and reduces its own slice of the
+    layer output, the per-row absmax slices are exchanged and each rank
+    quantizes its slice with the row's global scale into every rank's code
+    buffer; the first layer quantizes the replicated input locally and the
+    last layer's fp16 output is gathered by the fused GEMM epilogue (on one
+    rank it is the plain fused chain).  Both modes are bit-identical to the
+    same chain of single-GPU fused linears.
+    Every rank's shard widths must be multiples of the rotation block (and
+    of 64) in int8 mode."""
 
     def __init__(self, blocks, *, group=None, rotation_block=128, out_dtype=torch.float16, peers=None,
-                 gather="auto"):
+                 gather="auto", activations="fp16", codes=None):
+        if activations not in ("fp16", "int8"):
+            raise ValueError("activations must be 'fp16' or 'int8'")
         self.hidden = blocks[0][1][0].shape[0]
-        self.layers = [[ColumnParallelLinear.from_full(wq, sw, None, group=group, rotation_block=rotation_block,
-                                                       out_dtype=out_dtype, peers=peers, gather=gather)
-                        for wq, sw in blk] for blk in blocks]
+        world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if activations == "int8" and world == 1:
+            activations = "fp16"               # one rank: nothing to exchange, the plain fused chain
+        self.activations = activations
+        if activations == "fp16":
+            self.layers = [[ColumnParallelLinear.from_full(wq, sw, None, group=group,
+                                                           rotation_block=rotation_block, out_dtype=out_dtype,
+                                                           peers=peers, gather=gather)
+                            for wq, sw in blk] for blk in blocks]
+            return
+        if codes is None or peers is None:
+            raise ValueError("activations='int8' needs codes=ActivationExchange and peers=PeerGather")
+        if out_dtype != torch.float16:
+            raise ValueError("activations='int8' exchanges fp16 layer outputs")
+        self.codes, self.peers = codes, peers
+        self.world, self.rank = codes.world, codes.rank
+        self.block = rotation_block
+        h = self.hidden
+        self.chain = []                        # (w shard, w_scale shard, K, N shard, col0, next-input range)
+        flat = [(wq, sw) for blk in blocks for wq, sw in blk]
+        nxt = [(0, h), (0, h), (0, 4 * h), (0, h)]
+        for i, (wq, sw) in enumerate(flat):
+            n, k = wq.shape
+            if n % self.world:
+                raise ValueError("N must divide by the world size")
+            ns = n // self.world
+            c0 = self.rank * ns
+            if ns % 64 or (self.block and self.block > 1 and ns % self.block):
+                raise ValueError("int8 activations need shard widths that are multiples of the rotation block")
+            if k > codes.ldq:
+                raise ValueError("ActivationExchange k_max is smaller than a layer's K")
+            rng = None if i == len(flat) - 1 else nxt[i % 4]
+            self.chain.append((wq[c0:c0 + ns].contiguous(), sw[c0:c0 + ns].contiguous(), k, ns, c0, rng))
+        self._ys = {}
+
+    def _y(self, m, ns, device):
+        key = (m, ns)
+        if key not in self._ys:
+            self._ys[key] = torch.empty((m, ns), device=device, dtype=torch.float16)
+        return self._ys[key]
+
+    def _forward_int8(self, x):
+        lib, ex, g = nat.library(), self.codes, self.peers
+        dev = x.device
+        stream = nat.stream_ptr(dev)
+        x2 = _rows_2d(x)
+        m, k0 = x2.shape
+        if m > ex.m_max:
+            raise ValueError("more rows than the ActivationExchange holds")
+        if m * self.chain[-1][3] * self.world > g.capacity:
+            raise ValueError("output larger than the PeerGather buffers")
+        block = _block(self.block, k0)
+        cur = 0
+        nat.check(lib.b2_act_quant(x2.data_ptr(), nat.DTYPE_CODE[x.dtype], m, k0, x2.stride(0) if m > 1 else k0,
+                                   block, 0, ex.codes[cur].data_ptr(), ex.ldq, ex.scale.data_ptr(), stream),
+                  "b2_act_quant")
+        for w, sw, k, ns, c0, rng in self.chain:
+            if rng is None:                    # last layer: fp16 output gathered in the epilogue
+                n_total = ns * self.world
+                epoch, slot = g.next_slot()
+                nat.check(lib.b2_qgemm_gather(nat.KIND_I8, ex.codes[cur].data_ptr(), ex.ldq, ex.scale.data_ptr(),
+                                              w.data_ptr(), k, m, ns, k, sw.data_ptr(), ns, None, 0,
+                                              EPILOGUES["separate"], nat.F16, n_total, c0, self.world, self.rank,
+                                              g.outs[slot], g.states, epoch, stream), "b2_qgemm_gather")
+                g.wait(epoch, stream)
+                return g.local[slot][: m * n_total].view(m, n_total).reshape(*x.shape[:-1], n_total)
+            y = self._y(m, ns, dev)
+            nat.check(lib.b2_qgemm(nat.KIND_I8, ex.codes[cur].data_ptr(), ex.ldq, w.data_ptr(), k, m, ns, k,
+                                   ex.scale.data_ptr(), sw.data_ptr(), ns, None, 0, EPILOGUES["separate"],
+                                   y.data_ptr(), nat.F16, ns, stream), "b2_qgemm")
+            lo, hi = rng
+            a, b = shard_overlap(c0, ns, lo, hi)
+            ex.exchange_slice(y.data_ptr() + (a - c0) * 2 if b > a else y.data_ptr(), m, b - a, ns,
+                              _block(self.block, hi - lo), 1 - cur, a - lo, stream)
+            cur = 1 - cur
+        raise AssertionError("unreachable")
 
     def forward(self, x):
+        if self.activations == "int8":
+            return self._forward_int8(x)
         h = self.hidden
         for qkv_l, out_l, up_l, down_l in self.layers:
             qkv = qkv_l(x)

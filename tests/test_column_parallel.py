@@ -195,6 +195,32 @@ def _peer_worker(rank, world, port, q):
             stack = ColumnParallelStack(blocks, peers=g, gather=mode)
             ys = stack(x0)
             ok_stack &= bool(torch.equal(ys.view(torch.int16), yr.view(torch.int16)))
+        # the same chain with INT8 activations exchanged between the layers
+        # (hidden 128 * world: every shard width a multiple of the block)
+        from rdna2_ops.column_parallel import ActivationExchange
+        hid8, blocks8 = 128 * world, []
+        for _ in range(2):
+            blk = []
+            for nn_, kk in ((3 * hid8, hid8), (hid8, hid8), (4 * hid8, hid8), (hid8, 4 * hid8)):
+                wf = torch.randn((nn_, kk), generator=gen, device="cuda") / kk ** 0.5
+                blk.append(qlinear.quantize_weight(wf, rotation_block=128))
+            blocks8.append(blk)
+        x8 = torch.randn((300, hid8), generator=gen, device="cuda").half()
+        yr8 = x8
+        for blk in blocks8:
+            (q1, s1), (q2, s2), (q3, s3), (q4, s4) = blk
+            qkv = w8a8_linear(yr8, q1, s1, rotation_block=128, out_dtype=torch.float16)
+            o = w8a8_linear(qkv[:, :hid8], q2, s2, rotation_block=128, out_dtype=torch.float16)
+            yr8 = w8a8_linear(w8a8_linear(o, q3, s3, rotation_block=128, out_dtype=torch.float16), q4, s4,
+                              rotation_block=128, out_dtype=torch.float16)
+        ex = ActivationExchange(300, 4 * hid8)
+        try:
+            stack8 = ColumnParallelStack(blocks8, peers=g, activations="int8", codes=ex)
+            for _ in range(3):                      # buffers and epochs reused across calls
+                y8 = stack8(x8)
+                ok_stack &= bool(torch.equal(y8.view(torch.int16), yr8.view(torch.int16)))
+        finally:
+            ex.close()
         from rdna2_ops import _native as nat
         q.put((rank, ok, ok_stack, nat.device_status()))
     finally:
@@ -209,7 +235,8 @@ def test_peer_gather_column_parallel_bit_identical():
     """Every rank's reassembled output (the gather inside the GEMM epilogue,
     or by copy engines behind a chunked GEMM, over NVLink) equals the
     single-GPU fused linear bit for bit, over several calls; a 2-block
-    column-parallel DiT stack equals the 1-GPU stack with either gather."""
+    column-parallel DiT stack equals the 1-GPU stack with either gather and
+    with INT8 activations exchanged between the layers."""
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs 2 GPUs")
@@ -224,3 +251,12 @@ def test_peer_gather_column_parallel_bit_identical():
         assert p.exitcode == 0
     res = sorted(q.get(timeout=10) for _ in range(world))
     assert all(ok and ok_stack and st == 0 for _, ok, ok_stack, st in res), res
+
+
+def test_shard_overlap_ranges():
+    from rdna2_ops.column_parallel import shard_overlap
+    assert shard_overlap(0, 768, 0, 512) == (0, 512)
+    assert shard_overlap(768, 768, 0, 512) == (512, 512)         # past the range: empty, at its end
+    assert shard_overlap(0, 512, 512, 2048) == (512, 512)        # before the range: empty, at its start
+    assert shard_overlap(2304, 1152, 0, 3072) == (2304, 3072)
+    assert shard_overlap(1024, 512, 512, 2048) == (1024, 1536)
