@@ -60,7 +60,7 @@ def parse():
                          "overlapped with a chunked GEMM (ce)")
     ap.add_argument("--gather-store", choices=("auto", "sm", "tma"), default="auto",
                     help="transport of the fused gather's peer copies: SM stores or TMA stores")
-    ap.add_argument("--activations", choices=("fp16", "int8"), default="fp16",
+    ap.add_argument("--activations", choices=("fp16", "int8"), default="int8",
                     help="c5 column-parallel stack: gather every fp16 layer output, or exchange only the next "
                          "layer's INT8 input codes")
     ap.add_argument("--column-parallel", action="store_true",
