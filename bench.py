@@ -63,6 +63,8 @@ def parse():
     ap.add_argument("--activations", choices=("fp16", "int8"), default="int8",
                     help="c5 column-parallel stack: gather every fp16 layer output, or exchange only the next "
                          "layer's INT8 input codes")
+    ap.add_argument("--exchange-two-launch", action="store_true",
+                    help="c5 INT8 exchange: the two phases as separate kernels instead of one cooperative launch")
     ap.add_argument("--column-parallel", action="store_true",
                     help="c5 on one GPU through the column-parallel stack (the N > 1 code path, eager calls)")
     ap.add_argument("--workload", default="c2",
@@ -923,7 +925,7 @@ def run_c5_multi(args, rank, world, local_rank):
     g = PeerGather(m * 4 * hid, torch.float16)
     ex = None
     if args.activations == "int8":
-        ex = ActivationExchange(m, 4 * hid)
+        ex = ActivationExchange(m, 4 * hid, fused=not args.exchange_two_launch)
         stack = ColumnParallelStack(blocks, peers=g, activations="int8", codes=ex)
     else:
         stack = ColumnParallelStack(blocks, peers=g, gather="ce" if args.gather == "ce" else "peer")
@@ -967,7 +969,7 @@ def run_c5_multi(args, rank, world, local_rank):
         cols = (hid + hid + 4 * hid + hid) * nblocks - hid
         recv = (world - 1) / world * m * cols + (world - 1) / world * m * hid * 2 \
             + (world - 1) * m * 4 * (4 * nblocks - 1)
-        stack_launches = 1 + 5 * (4 * nblocks - 1) + 2
+        stack_launches = 1 + (5 if args.exchange_two_launch else 3) * (4 * nblocks - 1) + 2
     elif args.gather == "ce":
         rows = -(-(-(-m // ce_chunks(world))) // 256) * 256
         stack_launches = 4 * nblocks * (2 * -(-m // rows) + (world - 1 if world > 1 else 0) + 1)
@@ -993,6 +995,8 @@ def run_c5_multi(args, rank, world, local_rank):
                          "frac": round(max(recv / 770e9 * 1e3,
                                            flops / world / (2.0 * peaks()["bf16_tflops"] * 1e12) * 1e3) / ms, 4)},
             "gpu_launches": stack_launches * steps, "gather": args.gather, "activations": args.activations,
+            "exchange": None if args.activations != "int8" else (
+                "two launches per layer" if args.exchange_two_launch else "one cooperative launch per layer"),
             "gather_store": args.gather_store if args.gather != "ce" else None, "clocks": clocks.summary(),
             "device_status": status,
             "timing": "eager public ColumnParallelStack calls"}

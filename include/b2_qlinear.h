@@ -329,6 +329,21 @@ int b2_shard_codes(const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ld
                    int world, int rank, const void* xchg_local, void* const* q_outs, int64_t ldq, int64_t col0,
                    float* scale, void* const* states, uint32_t epoch, void* stream);
 
+/* b2_shard_amax, b2_gather_wait on the phase-1 state and b2_shard_codes in
+ * one cooperative launch: every CTA of the grid is resident, runs the
+ * absmax pass, signals, waits (bounded, 2 s) for every rank's absmax slots
+ * of epoch_amax, then runs the codes pass and releases epoch_codes into
+ * every rank's phase-2 state.  Same arguments and results as the three
+ * calls (xchg holds every rank's exchange buffer; this rank's own is
+ * xchg[rank]); wait with b2_gather_wait on the phase-2 state.  A slice with
+ * Ns == 0 runs the three calls.  Only one rank per GPU: ranks sharing a
+ * device would wait on one another inside their kernels.  No reference
+ * counterpart. */
+int b2_shard_exchange(const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block, int quant,
+                      int world, int rank, void* const* xchg, void* const* amax_states, uint32_t epoch_amax,
+                      void* const* q_outs, int64_t ldq, int64_t col0, float* scale, void* const* code_states,
+                      uint32_t epoch_codes, void* stream);
+
 /* Copy-engine copy of `rows` rows of `width_bytes` bytes between two device
  * buffers that may live on different GPUs (an IPC-mapped peer pointer, for
  * instance): the copy-engine counterpart of the gather, used to measure the

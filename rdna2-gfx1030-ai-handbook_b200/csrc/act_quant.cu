@@ -318,21 +318,56 @@ constexpr int kLaneThreads = 384;
 constexpr int kLaneFull = 0;
 constexpr int kLaneAmax = 1;
 constexpr int kLaneCodes = 2;
+constexpr int kLaneFused = 3;
 
 // End of a sharded-mode launch, run by every thread: orders this thread's
 // peer stores, counts the CTA, and the last CTA releases the epoch into slot
 // `rank` of every rank's flag array and rearms the counter.
-__device__ __forceinline__ void shard_signal(const ShardArgs& sh) {
+__device__ __forceinline__ void shard_signal_to(int world, uint32_t* const* flag_slot, uint32_t* done_count,
+                                                uint32_t epoch) {
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    const uint32_t prev = atomicAdd(sh.done_count, 1u);
+    const uint32_t prev = atomicAdd(done_count, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();
-      for (int r = 0; r < sh.world; ++r) st_release_sys(sh.flag_slot[r], sh.epoch);
-      *sh.done_count = 0u;
+      for (int r = 0; r < world; ++r) st_release_sys(flag_slot[r], epoch);
+      *done_count = 0u;
     }
   }
+}
+
+__device__ __forceinline__ void shard_signal(const ShardArgs& sh) {
+  shard_signal_to(sh.world, sh.flag_slot, sh.done_count, sh.epoch);
+}
+
+// Fused mode, between the two passes: signal the absmax phase like
+// shard_signal, then wait (bounded, one thread per CTA) until every rank's
+// absmax slots for this epoch have arrived.  Needs every CTA of the grid
+// resident (cooperative launch): a waiting CTA never blocks one that has
+// yet to signal.  CTA-uniform result; false after the wait limit (status
+// 0x100 | kSiteGather).
+__device__ __forceinline__ bool shard_barrier(const ShardArgs& sh) {
+  __shared__ int s_ok;
+  shard_signal(sh);
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t start = globaltimer();
+    for (int r = 0; r < sh.world && ok; ++r) {
+      for (uint32_t i = 0;; ++i) {
+        if (static_cast<int32_t>(ld_acquire_sys(sh.own_flags + r) - sh.epoch) >= 0) break;
+        if ((i & 255u) == 255u && globaltimer() - start > kWaitLimitNs) {
+          if (sh.status != nullptr) atomicCAS(sh.status, 0, 0x100 | kSiteGather);
+          ok = 0;
+          break;
+        }
+        __nanosleep(64);
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
 }
 
 // A sharded launch whose slice is empty (this rank holds none of the next
@@ -448,6 +483,20 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
   if constexpr (kPrefetch) issue(static_cast<int64_t>(blockIdx.x) * rows_per_cta);
   __syncthreads();
   int it = 0;
+  constexpr bool kFused = MODE == kLaneFused;
+  bool fused_ok = true;  // CTA-uniform: the barrier between the passes completed
+  for (int pass = 0; pass < (kFused ? 2 : 1); ++pass) {
+  // amax pass: the slice's row maxima to every rank; codes pass: codes with
+  // the row's global scale, staged and sent by bulk stores
+  const bool amax_pass = MODE == kLaneAmax || (kFused && pass == 0);
+  const bool codes_pass = MODE == kLaneCodes || (kFused && pass == 1);
+  if (kFused && pass == 1) {
+    if (!shard_barrier(sh)) {
+      fused_ok = false;  // no codes: release nothing, the peers' waits give up too
+      break;
+    }
+    if constexpr (kPrefetch) issue(static_cast<int64_t>(blockIdx.x) * rows_per_cta);
+  }
   for (int64_t base = static_cast<int64_t>(blockIdx.x) * rows_per_cta; base < M; base += row_step, ++it) {
     const int64_t row = base + r_local;
     const bool live = active && row < M;
@@ -522,11 +571,11 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
     const int sb = it % 3;
     if (live) atomicMax(&s_max[sb][r_local], __float_as_uint(amax));
     for (int i = tid; i < rows_per_cta; i += blockDim.x) s_max[(it + 1) % 3][i] = 0u;  // next iteration's
-    if constexpr (MODE == kLaneCodes) {
+    if (codes_pass) {
       if (part == 0 && active) bulk_wait_read<0>();  // this iteration's buffer is free again
     }
     __syncthreads();
-    if constexpr (MODE == kLaneCodes) {
+    if (codes_pass) {
       if (part == 0 && active) {
         if (staged_row >= 0) send_row((it + 1) & 1);
         staged_row = live ? row : -1;
@@ -534,12 +583,12 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
     }
     if (!live) continue;
     amax = __uint_as_float(s_max[sb][r_local]);
-    if constexpr (MODE == kLaneAmax) {
+    if (amax_pass) {
       if (part == 0)
         for (int r = 0; r < sh.world; ++r) sh.xchg[r][static_cast<int64_t>(sh.rank) * M + row] = amax;
       continue;
     }
-    if constexpr (MODE == kLaneCodes) {
+    if (codes_pass) {
       amax = 0.0f;
       for (int r = 0; r < sh.world; ++r) amax = fmaxf(amax, sh.xlocal[static_cast<int64_t>(r) * M + row]);
     }
@@ -549,7 +598,7 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
     uint8_t* dst = q + row * ldq + static_cast<int64_t>(part) * E;
     uint8_t* stage = s_stage + ((it & 1) * rows_per_cta + r_local) * K + part * E;
     auto put = [&](int j, const uint4& v) {
-      if constexpr (MODE == kLaneCodes) {
+      if (codes_pass) {
         *reinterpret_cast<uint4*>(stage + 16 * j) = v;
       } else {
         *reinterpret_cast<uint4*>(dst + 16 * j) = v;
@@ -634,9 +683,10 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
       }
     }
     if (part == 0) scale[row] = sc;
-    if constexpr (MODE == kLaneCodes) fence_proxy_async_smem();  // staged codes visible to the bulk stores
+    if (codes_pass) fence_proxy_async_smem();  // staged codes visible to the bulk stores
   }
-  if constexpr (MODE == kLaneCodes) {
+  }
+  if constexpr (MODE == kLaneCodes || kFused) {
     __syncthreads();
     if (part == 0 && active) {
       if (staged_row >= 0) send_row((it + 1) & 1);
@@ -644,7 +694,11 @@ __global__ void __launch_bounds__(kLaneThreads, 1)
       fence_proxy_async_global();
     }
   }
-  if constexpr (MODE != kLaneFull) shard_signal(sh);
+  if constexpr (kFused) {
+    if (fused_ok) shard_signal_to(sh.world, sh.flag_slot2, sh.done_count2, sh.epoch2);
+  } else if constexpr (MODE != kLaneFull) {
+    shard_signal(sh);
+  }
 }
 
 // 0 automatic (the lane-block kernel where it applies, else the warp-shuffle
@@ -666,8 +720,8 @@ static cudaError_t launch_lane(int64_t M, cudaStream_t st, const void* x, int64_
   if (rows < 1) rows = 1;
   const int threads = (rows * tpr + 31) / 32 * 32;
   // kLaneCodes stages two buffers of rows x K code bytes (at most 48 KiB)
-  const size_t dyn = MODE == kLaneCodes ? static_cast<size_t>(2 * rows * K) : 0;
-  if (MODE == kLaneCodes) {
+  const size_t dyn = (MODE == kLaneCodes || MODE == kLaneFused) ? static_cast<size_t>(2 * rows * K) : 0;
+  if (MODE == kLaneCodes || MODE == kLaneFused) {
     static bool configured[64] = {false};
     int d = 0;
     cudaGetDevice(&d);
@@ -691,6 +745,16 @@ static cudaError_t launch_lane(int64_t M, cudaStream_t st, const void* x, int64_
   const int64_t need = (M + rows - 1) / rows;
   const int64_t cap = static_cast<int64_t>(device_sm_count()) * n;
   const unsigned grid = static_cast<unsigned>(need < cap ? need : cap);
+  if constexpr (MODE == kLaneFused) {
+    // every CTA resident at once: the CTAs wait for one another (through
+    // the other ranks) between the passes
+    int m32 = static_cast<int>(M);
+    void* args[] = {(void*)&x, (void*)&ldx, (void*)&m32, (void*)&K, (void*)&tpr, (void*)&rows, (void*)&block,
+                    (void*)&inv, (void*)&q, (void*)&ldq, (void*)&scale, (void*)&early, (void*)&sh};
+    cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kernel), dim3(grid), dim3(threads),
+                                                args, dyn, st);
+    return e != cudaSuccess ? e : cudaGetLastError();
+  }
   kernel<<<grid, threads, dyn, st>>>(x, ldx, static_cast<int>(M), K, tpr, rows, block, inv, q, ldq, scale, early,
                                      sh);
   return cudaGetLastError();
@@ -816,7 +880,8 @@ cudaError_t run_act_quant(const void* x, int x_dtype, int64_t M, int64_t K, int6
 cudaError_t run_shard_quant(int mode, const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block,
                             int quant, int64_t ldq, float* scale, const ShardArgs& sh, cudaStream_t stream) {
   if (M <= 0) return cudaSuccess;
-  if (mode != kLaneAmax && mode != kLaneCodes) return cudaErrorInvalidValue;
+  if (mode != kLaneAmax && mode != kLaneCodes && mode != kLaneFused) return cudaErrorInvalidValue;
+  if (mode == kLaneFused && Ns == 0) return cudaErrorInvalidValue;
   if (Ns == 0) {
     const int64_t blocks = (M + 255) / 256;
     const unsigned grid = static_cast<unsigned>(blocks < 1024 ? blocks : 1024);
@@ -831,7 +896,9 @@ cudaError_t run_shard_quant(int mode, const void* y, int y_dtype, int64_t M, int
 #define B2_SQ(DT, F)                                                                                        \
   return mode == kLaneAmax                                                                                  \
              ? launch_lane<DT, F, kLaneAmax>(M, stream, y, ldy, k, block, inv, nullptr, ldq, scale, 0, sh)  \
-             : launch_lane<DT, F, kLaneCodes>(M, stream, y, ldy, k, block, inv, nullptr, ldq, scale, 0, sh)
+         : mode == kLaneCodes                                                                               \
+             ? launch_lane<DT, F, kLaneCodes>(M, stream, y, ldy, k, block, inv, nullptr, ldq, scale, 0, sh) \
+             : launch_lane<DT, F, kLaneFused>(M, stream, y, ldy, k, block, inv, nullptr, ldq, scale, 0, sh)
 #define B2_SQ_DT(F)                  \
   switch (y_dtype) {                 \
     case kF32: B2_SQ(kF32, F);       \

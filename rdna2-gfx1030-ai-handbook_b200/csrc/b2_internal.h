@@ -29,6 +29,13 @@ struct ShardArgs {
   uint32_t* flag_slot[kMaxGatherPeers + 1] = {};
   uint32_t* done_count = nullptr;
   uint32_t epoch = 0;
+  // fused mode (absmax exchange, in-kernel barrier, codes): this rank's own
+  // absmax-phase flags to wait on, and the codes phase's signal
+  const uint32_t* own_flags = nullptr;
+  uint32_t* flag_slot2[kMaxGatherPeers + 1] = {};
+  uint32_t* done_count2 = nullptr;
+  uint32_t epoch2 = 0;
+  int* status = nullptr;  // the bounded-wait status word
 };
 
 struct GemmParams {
@@ -103,8 +110,10 @@ int pair_capacity();
 // GEMM, launched with programmatic serialization) start its setup and
 // weight loads while this one runs; only for callers whose next kernel reads
 // nothing else this kernel's predecessors may still write.
-// One sharded prologue launch (mode 1 = amax exchange, 2 = codes) over a
-// column slice [M, Ns] of 16/32-bit activations; Ns may be 0.
+// One sharded prologue launch (mode 1 = amax exchange, 2 = codes, 3 = both
+// with an in-kernel cross-GPU barrier between them, cooperative launch)
+// over a column slice [M, Ns] of 16/32-bit activations; Ns may be 0 for
+// modes 1 and 2.
 cudaError_t run_shard_quant(int mode, const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block,
                             int quant, int64_t ldq, float* scale, const ShardArgs& sh, cudaStream_t stream);
 

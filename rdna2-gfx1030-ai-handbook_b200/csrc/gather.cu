@@ -495,3 +495,45 @@ extern "C" int b2_shard_codes(const void* y, int y_dtype, int64_t M, int64_t Ns,
   return static_cast<int>(b2::run_shard_quant(2, y, y_dtype, M, Ns, ldy, block, quant, ldq, scale, sh,
                                               static_cast<cudaStream_t>(stream)));
 }
+
+// Both exchange phases in one cooperative launch: the absmax pass, an
+// in-kernel barrier on every rank's absmax flags (bounded), then the codes
+// pass.  A rank whose slice is empty runs the two-launch form instead.
+extern "C" int b2_shard_exchange(const void* y, int y_dtype, int64_t M, int64_t Ns, int64_t ldy, int block,
+                                 int quant, int world, int rank, void* const* xchg, void* const* amax_states,
+                                 uint32_t epoch_amax, void* const* q_outs, int64_t ldq, int64_t col0, float* scale,
+                                 void* const* code_states, uint32_t epoch_codes, void* stream) {
+  int st = shard_checks(y, y_dtype, M, Ns, ldy, block, world, rank, amax_states, epoch_amax);
+  if (st == 0) st = shard_checks(y, y_dtype, M, Ns, ldy, block, world, rank, code_states, epoch_codes);
+  if (st != 0) return st;
+  if (quant != 0 && quant != 1) return fail();
+  if (!xchg || !q_outs || !scale || reinterpret_cast<uintptr_t>(scale) % 4 != 0) return fail();
+  if (col0 < 0 || ldq % 16 != 0 || col0 % 16 != 0 || col0 + Ns > ldq) return fail();
+  for (int q = 0; q < world; ++q) {
+    if (!xchg[q] || reinterpret_cast<uintptr_t>(xchg[q]) % 4 != 0) return fail();
+    if (!q_outs[q] || !aligned16(q_outs[q])) return fail();
+  }
+  if (M == 0) return 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (Ns == 0) {
+    st = b2_shard_amax(y, y_dtype, M, Ns, ldy, block, world, rank, xchg, amax_states, epoch_amax, stream);
+    if (st == 0) st = b2_gather_wait(amax_states[rank], world, epoch_amax, stream);
+    if (st == 0)
+      st = b2_shard_codes(y, y_dtype, M, Ns, ldy, block, quant, world, rank, xchg[rank], q_outs, ldq, col0, scale,
+                          code_states, epoch_codes, stream);
+    return st;
+  }
+  b2::ShardArgs sh;
+  shard_signal_args(sh, world, rank, amax_states, epoch_amax);
+  for (int q = 0; q < world; ++q) {
+    sh.xchg[q] = static_cast<float*>(xchg[q]);
+    sh.qout[q] = static_cast<uint8_t*>(q_outs[q]) + col0;
+    sh.flag_slot2[q] = static_cast<uint32_t*>(code_states[q]) + rank;
+  }
+  sh.xlocal = static_cast<const float*>(xchg[rank]);
+  sh.own_flags = static_cast<const uint32_t*>(amax_states[rank]);
+  sh.done_count2 = reinterpret_cast<uint32_t*>(static_cast<char*>(code_states[rank]) + kCounterOffset);
+  sh.epoch2 = epoch_codes;
+  sh.status = b2::status_word_ptr();
+  return static_cast<int>(b2::run_shard_quant(3, y, y_dtype, M, Ns, ldy, block, quant, ldq, scale, sh, s));
+}

@@ -77,6 +77,9 @@ SIGNATURES = {
     "b2_gather_wait_ce": ([_p, _int, _int, _p], _int),
     "b2_shard_amax": ([_p, _int, _i64, _i64, _i64, _int, _int, _int, ctypes.POINTER(_p), ctypes.POINTER(_p),
                        ctypes.c_uint32, _p], _int),
+    "b2_shard_exchange": ([_p, _int, _i64, _i64, _i64, _int, _int, _int, _int, ctypes.POINTER(_p), ctypes.POINTER(_p),
+                           ctypes.c_uint32, ctypes.POINTER(_p), _i64, _i64, _p, ctypes.POINTER(_p), ctypes.c_uint32,
+                           _p], _int),
     "b2_shard_codes": ([_p, _int, _i64, _i64, _i64, _int, _int, _int, _int, _p, ctypes.POINTER(_p), _i64, _i64,
                         _p, ctypes.POINTER(_p), ctypes.c_uint32, _p], _int),
     "b2_quant_linear_noalloc_max_bytes": ([], _size),

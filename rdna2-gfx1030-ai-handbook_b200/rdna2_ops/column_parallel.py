@@ -167,10 +167,13 @@ class ActivationExchange:
     round16(k_max)] int8 that the peers write into, the row scales [m_max]
     (local) and one completion state per phase, all mapped by every peer
     like PeerGather's buffers.  `close()` is collective like
-    PeerGather.close."""
+    PeerGather.close.  fused=True runs both phases of an exchange in one
+    cooperative kernel (b2_shard_exchange; one rank per GPU), False as two
+    kernels with a wait between them."""
 
-    def __init__(self, m_max, k_max, *, group=None, device=None, exchange=None):
+    def __init__(self, m_max, k_max, *, group=None, device=None, exchange=None, fused=True):
         self.group = group
+        self.fused = bool(fused)
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.device = device or torch.device("cuda", torch.cuda.current_device())
@@ -211,15 +214,21 @@ class ActivationExchange:
         lib = self.lib
         ptr = y if isinstance(y, int) else y.data_ptr()
         self.epoch_amax += 1
-        nat.check(lib.b2_shard_amax(ptr, nat.F16, m, width, ldy, block, self.world, self.rank, self.xchg_ptrs,
-                                    self.amax_states, self.epoch_amax, stream), "b2_shard_amax")
-        nat.check(lib.b2_gather_wait(self.state_amax.data_ptr(), self.world, self.epoch_amax, stream),
-                  "b2_gather_wait")
         self.epoch_codes += 1
-        nat.check(lib.b2_shard_codes(ptr, nat.F16, m, width, ldy, block, 0, self.world, self.rank,
-                                     self.xchg.data_ptr(), self.code_ptrs[dst], self.ldq, col0,
-                                     self.scale.data_ptr(), self.code_states, self.epoch_codes, stream),
-                  "b2_shard_codes")
+        if self.fused:                         # both phases in one cooperative launch
+            nat.check(lib.b2_shard_exchange(ptr, nat.F16, m, width, ldy, block, 0, self.world, self.rank,
+                                            self.xchg_ptrs, self.amax_states, self.epoch_amax, self.code_ptrs[dst],
+                                            self.ldq, col0, self.scale.data_ptr(), self.code_states,
+                                            self.epoch_codes, stream), "b2_shard_exchange")
+        else:
+            nat.check(lib.b2_shard_amax(ptr, nat.F16, m, width, ldy, block, self.world, self.rank,
+                                        self.xchg_ptrs, self.amax_states, self.epoch_amax, stream), "b2_shard_amax")
+            nat.check(lib.b2_gather_wait(self.state_amax.data_ptr(), self.world, self.epoch_amax, stream),
+                      "b2_gather_wait")
+            nat.check(lib.b2_shard_codes(ptr, nat.F16, m, width, ldy, block, 0, self.world, self.rank,
+                                         self.xchg.data_ptr(), self.code_ptrs[dst], self.ldq, col0,
+                                         self.scale.data_ptr(), self.code_states, self.epoch_codes, stream),
+                      "b2_shard_codes")
         nat.check(lib.b2_gather_wait(self.state_codes.data_ptr(), self.world, self.epoch_codes, stream),
                   "b2_gather_wait")
 

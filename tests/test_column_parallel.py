@@ -213,14 +213,15 @@ def _peer_worker(rank, world, port, q):
             o = w8a8_linear(qkv[:, :hid8], q2, s2, rotation_block=128, out_dtype=torch.float16)
             yr8 = w8a8_linear(w8a8_linear(o, q3, s3, rotation_block=128, out_dtype=torch.float16), q4, s4,
                               rotation_block=128, out_dtype=torch.float16)
-        ex = ActivationExchange(300, 4 * hid8)
-        try:
-            stack8 = ColumnParallelStack(blocks8, peers=g, activations="int8", codes=ex)
-            for _ in range(3):                      # buffers and epochs reused across calls
-                y8 = stack8(x8)
-                ok_stack &= bool(torch.equal(y8.view(torch.int16), yr8.view(torch.int16)))
-        finally:
-            ex.close()
+        for fused in (True, False):                 # one-launch and two-launch exchanges
+            ex = ActivationExchange(300, 4 * hid8, fused=fused)
+            try:
+                stack8 = ColumnParallelStack(blocks8, peers=g, activations="int8", codes=ex)
+                for _ in range(3):                  # buffers and epochs reused across calls
+                    y8 = stack8(x8)
+                    ok_stack &= bool(torch.equal(y8.view(torch.int16), yr8.view(torch.int16)))
+            finally:
+                ex.close()
         from rdna2_ops import _native as nat
         q.put((rank, ok, ok_stack, nat.device_status()))
     finally:

@@ -162,3 +162,29 @@ def test_shard_rejects_bad_calls():
     assert lib.b2_shard_codes(*args, 128, 256, 128, 3, 2, 0, vx.xchg[0].data_ptr(), vx.codes_p, 256, 0,
                               vx.scale[0].data_ptr(), vx.st_c_p, 1, None) != 0                 # quant
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("ns,lo,hi,block,dtype,m", [(1536, 0, 1536, 128, torch.float16, 300),
+                                                    (3072, 0, 1024, 256, torch.bfloat16, 77),
+                                                    (12288, 0, 12288, 128, torch.float16, 513)])
+def test_shard_exchange_fused_one_rank(ns, lo, hi, block, dtype, m):
+    """The one-launch exchange (absmax pass, in-kernel barrier, codes pass)
+    on a single rank -- the only form one GPU may run, since ranks sharing a
+    device would wait on each other inside their kernels -- equals the
+    whole-row prologue bit for bit over two calls."""
+    rng = np.random.default_rng(ns + m)
+    y = torch.from_numpy(outlier_activations(rng, m, ns)).to(dtype).cuda()
+    ref_q, ref_s = qlinear.act_quant(y[:, lo:hi], rotation_block=block)
+    ldq = -(-(hi - lo) // 16) * 16
+    vx = VirtualExchange(1, m, ldq)
+    lib = nat.library()
+    for epoch in (1, 2):
+        vx.codes[0].fill_(0x55)
+        nat.check(lib.b2_shard_exchange(y[:, lo:].data_ptr(), nat.DTYPE_CODE[dtype], m, hi - lo, ns, block, 0, 1, 0,
+                                        vx.xchg_p, vx.st_a_p, epoch, vx.codes_p, ldq, 0, vx.scale[0].data_ptr(),
+                                        vx.st_c_p, epoch, nat.stream_ptr(y.device)), "b2_shard_exchange")
+        nat.check(lib.b2_gather_wait(vx.st_c[0].data_ptr(), 1, epoch, nat.stream_ptr(y.device)), "b2_gather_wait")
+        torch.cuda.synchronize()
+        assert torch.equal(vx.codes[0][:, :hi - lo], ref_q), epoch
+        assert torch.equal(vx.scale[0].view(torch.int32), ref_s.view(torch.int32)), epoch
+    assert nat.device_status() == 0
