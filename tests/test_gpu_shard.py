@@ -188,3 +188,24 @@ def test_shard_exchange_fused_one_rank(ns, lo, hi, block, dtype, m):
         assert torch.equal(vx.codes[0][:, :hi - lo], ref_q), epoch
         assert torch.equal(vx.scale[0].view(torch.int32), ref_s.view(torch.int32)), epoch
     assert nat.device_status() == 0
+
+
+def test_shard_exchange_barrier_gives_up_when_a_rank_never_comes():
+    """Rank 0 of two runs the one-launch exchange; rank 1 never does, so its
+    absmax slots never arrive.  Every CTA's in-kernel wait ends after its
+    2 s bound with status 0x107, no codes phase runs and nothing is
+    released; the context still runs a linear afterwards."""
+    nat.device_status(reset=True)
+    lib = nat.library()
+    m, ns = 64, 256
+    vx = VirtualExchange(2, m, 2 * ns)
+    y = torch.ones((m, ns), device="cuda", dtype=torch.float16)
+    nat.check(lib.b2_shard_exchange(y.data_ptr(), nat.F16, m, ns, ns, 128, 0, 2, 0, vx.xchg_p, vx.st_a_p, 1,
+                                    vx.codes_p, 2 * ns, 0, vx.scale[0].data_ptr(), vx.st_c_p, 1,
+                                    nat.stream_ptr(y.device)), "b2_shard_exchange")
+    torch.cuda.synchronize()
+    assert nat.device_status(reset=True) == 0x107
+    assert int(vx.st_c[1].view(torch.int32)[0]) == 0            # no codes released to the other rank
+    assert torch.isfinite(rdna2_ops.w8a8_linear(y, torch.ones((64, ns), device="cuda", dtype=torch.int8),
+                                                torch.ones(64, device="cuda"), out_dtype=torch.float32)).all()
+    assert nat.device_status() == 0
